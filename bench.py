@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Benchmark of the decode-step hot path (one JSON line on rank 0).
+
+Headline workload: split-KV decode attention with ragged lengths (config 2:
+B=64, Hq=32, Hkv=8, D=128, cache padded to 32768, lengths ~U[512, 32768] from
+seed 1), one step = pass 1 + pass 2 over the whole batch. Metric: KV-read
+TB/s = algorithmic KV bytes (4096 B x sum of true lengths) / step time.
+The KV cache (4.4 GB of true KV, 17 GB padded) is larger than L2, so no flush
+is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun: rows are balanced across ranks by length (no
+collective on the data path); the step time is the max over ranks.
+``--impl reference`` times the reference's torch formulas on the host CPU
+(the oracle port; the reference's own kernels are sm_90a-only) on a bounded
+sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+# DRAM bytes (read + write) per launch of splitkv_fwd_kernel, from the ncu
+# capture summarised in profiles/splitkv_fwd_kernel_config2.md (None until captured).
+NCU_TRAFFIC_BYTES_PER_LAUNCH = None
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sms.append(float(f[0]))
+                maxes.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from fused_kernels_cutedsl_lib_b200 import (alloc_partials, chunk_tokens, configs,
+                                                dec_attn_splitkv_fwd, default_num_splits, _native)
+    from fused_kernels_cutedsl_lib_b200.sharding import balance_rows
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    cfg = configs.ATTN_CONFIG2
+    all_lens = configs.attn_seqlens(cfg)
+    rows = balance_rows(all_lens, world)[rank]
+    q, k, v, lens = configs.attn_inputs(cfg, device=dev, batch_rows=rows)
+    B = len(rows)
+    total_kv_bytes = cfg.kv_bytes(all_lens)
+    S = default_num_splits(B, cfg.num_heads_kv, cfg.max_seqlen, int(lens.sum()),
+                           num_sms=torch.cuda.get_device_properties(dev).multi_processor_count)
+    out = torch.empty(B, 1, cfg.num_heads_q, 128, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, cfg.num_heads_q, dtype=torch.float32, device=dev)
+    o_p, l_p = alloc_partials(B, cfg.num_heads_q, S, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, S)
+
+    def pass1_pass2_events(n):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+                torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        return evs
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, events per pass on the launching stream ----
+    evs = pass1_pass2_events(args.steps)
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    from fused_kernels_cutedsl_lib_b200.decoding_attention import dec_attn_combine, dec_attn_splitkv_partial
+    t_start.record(stream)
+    for i in range(args.steps):
+        e0, e1, e2 = evs[i]
+        e0.record(stream)
+        dec_attn_splitkv_partial(q, k, v, lens, o_p, l_p, S)
+        e1.record(stream)
+        dec_attn_combine(o_p, l_p, lens, out, lse, cfg.max_seqlen)
+        e2.record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    p1 = [a.elapsed_time(b) for a, b, _ in evs]
+    p2 = [b.elapsed_time(c) for _, b, c in evs]
+    local_ms = total_ms / args.steps
+    if _native.device_error() != 0:
+        raise RuntimeError("device error word set during the bench")
+
+    # ---- e2e: public API with pinned host buffers, copies inside the timed region ----
+    q_h = q.cpu().pin_memory()
+    lens_h = lens.cpu().pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    lse_h = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+    q_d = torch.empty_like(q)
+    lens_d = torch.empty_like(lens)
+    from fused_kernels_cutedsl_lib_b200 import DecodeAttention
+    attn = DecodeAttention(num_splits=S)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        lens_d.copy_(lens_h, non_blocking=True)
+        attn(q_d, k, v, lens_d, out, lse)
+        out_h.copy_(out, non_blocking=True)
+        lse_h.copy_(lse, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_local_ms = a.elapsed_time(b) / args.steps
+    h2d = q_h.numel() * q_h.element_size() + lens_h.numel() * 4
+    d2h = out_h.numel() * 2 + lse_h.numel() * 4
+
+    # ---- max over ranks ----
+    vals = torch.tensor([local_ms, e2e_local_ms, statistics.mean(p1), statistics.mean(p2)],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        hb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+        dist.all_reduce(hb, op=dist.ReduceOp.SUM)
+        h2d, d2h = int(hb[0]), int(hb[1])
+    step_ms, e2e_ms, p1_ms, p2_ms = vals.tolist()
+
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        tbps = total_kv_bytes / (step_ms * 1e-3) / 1e12
+        # Dominant kernel (pass 1) on one GPU: algorithmic bytes per launch / mean launch time.
+        local_kv = cfg.kv_bytes(lens.cpu()) + B * cfg.num_heads_q * 256
+        achieved_gbs = local_kv / (statistics.mean(p1) * 1e-3) / 1e9
+        line = {
+            "metric": "decode-attn KV-read TB/s (split-KV ragged, B=64, Lmax=32768, 32q/8kv, d128)",
+            "value": round(tbps, 4),
+            "unit": "TB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(step_ms, 5),
+            "us_per_call": round(step_ms * 1e3, 2),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k/v, lengths U[512,32768] seed 1)",
+            "config": {"workload": "splitkv_decode_attention_config2", "batch": cfg.batch,
+                       "max_seqlen": cfg.max_seqlen, "num_heads_q": cfg.num_heads_q,
+                       "num_heads_kv": cfg.num_heads_kv, "head_dim": 128, "num_splits": S,
+                       "chunk_tokens": chunk_tokens(cfg.max_seqlen, S),
+                       "sum_seqlens": int(all_lens.sum()), "kv_bytes": total_kv_bytes,
+                       "parallelism": f"batch-sharded x{world} (length-balanced, no collective)",
+                       "l2": "inputs (17 GB padded KV) larger than L2; no flush"},
+            "pass_ms": {"splitkv_fwd": round(p1_ms, 5), "combine": round(p2_ms, 5)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved_gbs / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "splitkv_fwd_kernel",
+                         "traffic": NCU_TRAFFIC_BYTES_PER_LAUNCH},
+            "e2e": {"value": round(total_kv_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "note": "q + cache_seqlens H2D from pinned host, out + lse D2H; KV cache resident"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, q, k, v, lens, budget_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(cfg, q, k, v, lens, budget_s=15.0):
+    """Time the reference's torch formulas (oracle port) on the host over a bounded sample of rows."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = list(range(q.shape[0]))
+    done_bytes, t_used, n = 0, 0.0, 0
+    for r in rows:
+        qr, kr, vr, lr = q[r:r + 1].cpu(), k[r:r + 1, :int(lens[r])].cpu(), v[r:r + 1, :int(lens[r])].cpu(), lens[r:r + 1].cpu()
+        t0 = time.perf_counter()
+        oracle.decode_attention(qr, kr, vr, lr)
+        t_used += time.perf_counter() - t0
+        done_bytes += int(lr[0]) * cfg.num_heads_kv * 128 * 4
+        n += 1
+        if t_used >= budget_s:
+            break
+    return {"value": round(done_bytes / t_used / 1e12, 6), "unit": "TB/s", "cores": threads,
+            "kind": "port", "sample": f"{n} of {cfg.batch} rows of config 2 ({done_bytes} KV bytes), "
+                                      f"fp32 torch on CPU, {t_used:.1f} s"}
+
+
+def run_reference(args):
+    """CPU arm: the reference's torch check formulas (oracle port) on the host cores."""
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    import oracle
+    from fused_kernels_cutedsl_lib_b200 import configs
+
+    cfg = configs.ATTN_CONFIG2
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    all_lens = configs.attn_seqlens(cfg)
+    # Bounded sample per step: two full rows (drawn on the CPU with the same per-row seeds).
+    rows = [0, 1]
+    q, k, v, lens = configs.attn_inputs(cfg, device="cpu", batch_rows=rows)
+    sample_bytes = cfg.kv_bytes(lens)
+
+    def step():
+        oracle.decode_attention(q, k, v, lens)
+
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.mean(times)
+    tbps = sample_bytes / sec / 1e12
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "decode-attn KV-read TB/s (split-KV ragged, B=64, Lmax=32768, 32q/8kv, d128)",
+        "value": round(tbps, 6), "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (same seeded rows as the GPU arm)",
+        "config": {"workload": "splitkv_decode_attention_config2", "sample_rows": rows,
+                   "sample_kv_bytes": sample_bytes, "sum_seqlens_full": int(all_lens.sum())},
+        "cpu_baseline": {"value": round(tbps, 6), "unit": "TB/s", "cores": threads, "kind": "port",
+                         "sample": f"rows {rows} of config 2 per step, fp32 torch on CPU"},
+        "e2e": {"value": round(tbps, 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

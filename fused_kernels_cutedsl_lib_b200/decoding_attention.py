@@ -1,0 +1,200 @@
+"""Split-KV decode attention (host side of ``csrc/dec_attn.cu``).
+
+Reference boundary: the reference exports its decode attention as a kernel
+object, ``DAttn1(qk_mnk, stages, p_stages, is_persistent)``, compiled by
+``compile_cutedsl`` into a callable over torch tensors
+(python/cutedsl_kernels/decoding_attention/attn1.py:70-90,
+python/cdsl_helpers/cdsl_fn_utils.py:38-44). The callable writes the
+caller-allocated output in place and returns ``None``. This module keeps that
+ownership and calling style for the split-KV decode path:
+
+* :func:`dec_attn_splitkv_fwd` — both passes (the C ABI ``fk_dec_attn_fwd``);
+* :func:`dec_attn_splitkv_partial` / :func:`dec_attn_combine` — pass 1 / pass 2;
+* :class:`DecodeAttention` — a kernel object in the reference's style whose
+  ``__call__(q, k_cache, v_cache, cache_seqlens, out, lse, softmax_scale)``
+  allocates the split partials itself (once, cached per shape).
+
+Semantics (softmax, GQA, natural-log LSE, empty rows) follow the reference's
+attention references ``attn_reimpl`` (attn/attempt6_epi_pipeline/attn.py:778-784)
+and SDPA (attn/attempt6_epi_pipeline/tests.py:85), with the zero-row-sum guard of
+attn/attempt6_epi_pipeline/my_softmax.py:88-97 (a row with no keys yields 0).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native
+from ._tensors import ptr, require_shape, require_tensor, same_device, stream_for
+
+HEAD_DIM = 128
+TILE_TOKENS = 64
+
+
+def chunk_tokens(max_seqlen: int, num_splits: int) -> int:
+    """Tokens per split: ceil(max_seqlen / num_splits) rounded up to 64."""
+    c = -(-max_seqlen // num_splits)
+    return -(-c // TILE_TOKENS) * TILE_TOKENS
+
+
+def default_num_splits(batch: int, num_heads_kv: int, max_seqlen: int,
+                       total_tokens: int | None = None, num_sms: int = 148,
+                       ctas_per_sm: int = 2) -> int:
+    """Pick num_splits so the work units fill the persistent grid evenly.
+
+    Units are (row, kv head, split) of ``chunk`` tokens. The chunk is the
+    largest of {1024, 512, 256, 128, 64} tokens that still yields >= 4 units
+    per resident CTA (so the round-robin deal is within ~25% of even in the
+    worst case and usually far better); ``total_tokens`` (sum of the true
+    lengths) sharpens the count for ragged batches.
+    """
+    total = total_tokens if total_tokens is not None else batch * max_seqlen
+    slots = num_sms * ctas_per_sm
+    chunk = TILE_TOKENS
+    for c in (1024, 512, 256, 128, 64):
+        units = num_heads_kv * max(1, -(-total // c))
+        if units >= 4 * slots:
+            chunk = c
+            break
+    return max(1, -(-max_seqlen // chunk))
+
+
+def _check_attn(q, k_cache, v_cache, cache_seqlens):
+    require_tensor("q", q, torch.bfloat16)
+    require_tensor("k_cache", k_cache, torch.bfloat16, 4)
+    require_tensor("v_cache", v_cache, torch.bfloat16, 4)
+    require_tensor("cache_seqlens", cache_seqlens, torch.int32, 1)
+    B, L, Hkv, D = k_cache.shape
+    require_shape("v_cache", v_cache, (B, L, Hkv, D))
+    if D != HEAD_DIM:
+        raise ValueError(f"head_dim must be {HEAD_DIM}, got {D}")
+    if q.dim() == 4:
+        if q.shape[1] != 1:
+            raise ValueError("decode attention takes one query token per row (q.shape[1] == 1)")
+        Hq = q.shape[2]
+    elif q.dim() == 3:
+        Hq = q.shape[1]
+    else:
+        raise ValueError(f"q must be [B, 1, Hq, D] or [B, Hq, D], got {tuple(q.shape)}")
+    if q.shape[0] != B or q.shape[-1] != D:
+        raise ValueError(f"q shape {tuple(q.shape)} does not match k_cache {tuple(k_cache.shape)}")
+    if Hq % Hkv != 0 or Hq // Hkv > 8:
+        raise ValueError(f"num_heads_q ({Hq}) must be a multiple of num_heads_kv ({Hkv}), ratio <= 8")
+    require_shape("cache_seqlens", cache_seqlens, (B,))
+    dev = same_device(q, k_cache, v_cache, cache_seqlens)
+    return B, L, Hq, Hkv, D, dev
+
+
+def alloc_partials(batch: int, num_heads_q: int, num_splits: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    o_partial = torch.empty((num_splits, batch, num_heads_q, HEAD_DIM), dtype=torch.float32, device=device)
+    lse_partial = torch.empty((num_splits, batch, num_heads_q), dtype=torch.float32, device=device)
+    return o_partial, lse_partial
+
+
+def _check_partials(o_partial, lse_partial, num_splits, B, Hq):
+    require_tensor("o_partial", o_partial, torch.float32, 4)
+    require_tensor("lse_partial", lse_partial, torch.float32, 3)
+    if o_partial.shape[0] < num_splits or tuple(o_partial.shape[1:]) != (B, Hq, HEAD_DIM):
+        raise ValueError(f"o_partial must be [>= {num_splits}, {B}, {Hq}, {HEAD_DIM}], got {tuple(o_partial.shape)}")
+    if lse_partial.shape[0] < num_splits or tuple(lse_partial.shape[1:]) != (B, Hq):
+        raise ValueError(f"lse_partial must be [>= {num_splits}, {B}, {Hq}], got {tuple(lse_partial.shape)}")
+    if o_partial.shape[0] != num_splits or lse_partial.shape[0] != num_splits:
+        raise ValueError("o_partial / lse_partial leading dim must equal num_splits")
+
+
+def dec_attn_splitkv_partial(q, k_cache, v_cache, cache_seqlens, o_partial, lse_partial,
+                             num_splits: int, softmax_scale: float | None = None, stream=None) -> None:
+    """Pass 1: write per-split normalised O (fp32) and natural-log LSE."""
+    B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
+    _check_partials(o_partial, lse_partial, num_splits, B, Hq)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    st = stream_for(dev, stream)
+    _native.check(_native.load().fk_dec_attn_splitkv_fwd(
+        ptr(q), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(o_partial), ptr(lse_partial),
+        B, L, Hq, Hkv, D, num_splits, scale, st))
+
+
+def dec_attn_combine(o_partial, lse_partial, cache_seqlens, out, lse, max_seqlen: int,
+                     stream=None) -> None:
+    """Pass 2: merge the splits of every (row, q head) into bf16 ``out`` and fp32 ``lse``."""
+    require_tensor("o_partial", o_partial, torch.float32, 4)
+    require_tensor("lse_partial", lse_partial, torch.float32, 3)
+    require_tensor("cache_seqlens", cache_seqlens, torch.int32, 1)
+    require_tensor("out", out, torch.bfloat16)
+    require_tensor("lse", lse, torch.float32, 2)
+    S, B, Hq, D = o_partial.shape
+    require_shape("lse_partial", lse_partial, (S, B, Hq))
+    if out.numel() != B * Hq * D:
+        raise ValueError(f"out must hold {B}x{Hq}x{D} elements, got shape {tuple(out.shape)}")
+    require_shape("lse", lse, (B, Hq))
+    dev = same_device(o_partial, lse_partial, cache_seqlens, out, lse)
+    st = stream_for(dev, stream)
+    _native.check(_native.load().fk_dec_attn_combine(
+        ptr(o_partial), ptr(lse_partial), ptr(cache_seqlens), ptr(out), ptr(lse),
+        B, int(max_seqlen), Hq, D, S, st))
+
+
+def dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_partial, lse_partial,
+                         num_splits: int, softmax_scale: float | None = None, stream=None) -> None:
+    """Both passes: ``out = softmax(q K^T * scale) V`` per row over its first ``cache_seqlens[b]`` keys."""
+    B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
+    _check_partials(o_partial, lse_partial, num_splits, B, Hq)
+    require_tensor("out", out, torch.bfloat16)
+    require_tensor("lse", lse, torch.float32, 2)
+    if out.numel() != B * Hq * D:
+        raise ValueError(f"out must hold {B}x{Hq}x{D} elements, got shape {tuple(out.shape)}")
+    require_shape("lse", lse, (B, Hq))
+    same_device(q, out, lse, o_partial, lse_partial)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    st = stream_for(dev, stream)
+    _native.check(_native.load().fk_dec_attn_fwd(
+        ptr(q), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), ptr(lse),
+        ptr(o_partial), ptr(lse_partial), B, L, Hq, Hkv, D, num_splits, scale, st))
+
+
+class DecodeAttention:
+    """Kernel object in the reference's style (cf. ``DAttn1(...)`` then a call).
+
+    ``DecodeAttention(num_splits=None)(q, k_cache, v_cache, cache_seqlens, out, lse,
+    softmax_scale)`` runs both passes, writing ``out``/``lse`` in place and
+    returning ``None``. Split partials are allocated once per (shape, device)
+    and reused; pass ``num_splits`` to pin the split count, else
+    :func:`default_num_splits` picks it from the padded length.
+    """
+
+    def __init__(self, num_splits: int | None = None):
+        self.num_splits = num_splits
+        self._ws: dict = {}
+
+    def splits_for(self, batch: int, num_heads_kv: int, max_seqlen: int) -> int:
+        if self.num_splits is not None:
+            return int(self.num_splits)
+        return default_num_splits(batch, num_heads_kv, max_seqlen)
+
+    def workspace(self, batch, num_heads_q, num_splits, device):
+        key = (batch, num_heads_q, num_splits, str(device))
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = alloc_partials(batch, num_heads_q, num_splits, device)
+            self._ws[key] = ws
+        return ws
+
+    def __call__(self, q, k_cache, v_cache, cache_seqlens, out, lse, softmax_scale=None,
+                 stream=None) -> None:
+        B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
+        S = self.splits_for(B, Hkv, L)
+        o_p, l_p = self.workspace(B, Hq, S, dev)
+        dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S,
+                             softmax_scale, stream)
+
+
+def decode_attention(q, k_cache, v_cache, cache_seqlens, softmax_scale=None, num_splits=None):
+    """Functional convenience: allocates ``out``/``lse``/partials, returns ``(out, lse)``."""
+    B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
+    S = num_splits if num_splits is not None else default_num_splits(B, Hkv, L)
+    out = torch.empty((B, 1, Hq, D), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
+    o_p, l_p = alloc_partials(B, Hq, S, dev)
+    dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, softmax_scale)
+    return out, lse

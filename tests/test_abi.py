@@ -1,0 +1,63 @@
+"""The C-ABI library loads and exports exactly what include/*.h declares (no GPU needed)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from fused_kernels_cutedsl_lib_b200 import _native
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        names |= set(re.findall(r"^FK_API\s+[\w\s\*]+?\b(fk_\w+)\s*\(", h.read_text(), flags=re.M))
+    return names
+
+
+def test_header_matches_binding_table():
+    assert _declared() == set(_native.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert lib.fk_version() == 1
+
+
+def test_argument_validation_before_launch():
+    lib = _native.load()
+    # head_dim 64 is rejected before anything touches CUDA
+    rc = lib.fk_dec_attn_splitkv_fwd(16, 16, 16, 16, 16, 16, 1, 64, 8, 2, 64, 1, 1.0, None)
+    assert rc == -1
+    assert "head_dim" in lib.fk_last_error().decode()
+    with pytest.raises(ValueError):
+        _native.check(rc)
+    # GQA group > 8
+    assert lib.fk_dec_attn_splitkv_fwd(16, 16, 16, 16, 16, 16, 1, 64, 16, 1, 128, 1, 1.0, None) == -1
+    # misaligned pointer
+    assert lib.fk_dec_attn_splitkv_fwd(18, 16, 16, 16, 16, 16, 1, 64, 8, 2, 128, 1, 1.0, None) == -1
+
+
+def test_chunk_rule():
+    lib = _native.load()
+    from fused_kernels_cutedsl_lib_b200 import chunk_tokens
+
+    for L, s in [(4096, 16), (32768, 64), (100, 3), (1, 1), (65, 1)]:
+        assert lib.fk_dec_attn_chunk_tokens(L, s) == chunk_tokens(L, s)
+        assert chunk_tokens(L, s) % 64 == 0
+
+
+def test_python_entry_points_reject_bad_tensors():
+    from fused_kernels_cutedsl_lib_b200 import decode_attention
+
+    q = torch.zeros(2, 1, 8, 128, dtype=torch.bfloat16)
+    k = torch.zeros(2, 16, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(TypeError):
+        decode_attention(q.float(), k, k, torch.zeros(2, dtype=torch.int32))
+    with pytest.raises(ValueError):  # CPU tensors
+        decode_attention(q, k, k, torch.zeros(2, dtype=torch.int32))

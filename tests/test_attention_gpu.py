@@ -1,0 +1,177 @@
+"""Parity of the split-KV decode attention kernels against the CPU oracle (GPU)."""
+import math
+
+import pytest
+import torch
+
+import oracle
+from fused_kernels_cutedsl_lib_b200 import (
+    DecodeAttention,
+    _native,
+    alloc_partials,
+    chunk_tokens,
+    dec_attn_combine,
+    dec_attn_splitkv_fwd,
+    dec_attn_splitkv_partial,
+    decode_attention,
+)
+from fused_kernels_cutedsl_lib_b200 import configs
+
+pytestmark = pytest.mark.gpu
+
+# Tolerances of the decode path: bf16 outputs vs an fp32 reference.
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+LSE_ABS = 1e-3
+
+
+def assert_attn_close(out, lse, ref_out, ref_lse, rows=None):
+    out = out.float().cpu().reshape(ref_out.shape[0] if rows is None else len(rows), -1, 128)
+    lse = lse.float().cpu()
+    if rows is not None:
+        out, lse = out, lse
+    err = (out - ref_out).abs()
+    assert err.max().item() <= MAX_ABS, f"max abs {err.max().item()}"
+    assert err.mean().item() <= MEAN_ABS, f"mean abs {err.mean().item()}"
+    fin = torch.isfinite(ref_lse)
+    assert torch.equal(torch.isfinite(lse), fin)
+    assert torch.all(torch.isneginf(lse[~fin]))
+    if fin.any():
+        lerr = (lse[fin] - ref_lse[fin]).abs().max().item()
+        assert lerr <= LSE_ABS, f"lse abs {lerr}"
+
+
+def run(q, k, v, lens, num_splits, scale=None):
+    B, L, Hkv, D = k.shape
+    Hq = q.shape[2]
+    out = torch.full((B, 1, Hq, D), float("nan"), dtype=torch.bfloat16, device=q.device)
+    lse = torch.full((B, Hq), float("nan"), dtype=torch.float32, device=q.device)
+    o_p, l_p = alloc_partials(B, Hq, num_splits, q.device)
+    o_p.fill_(float("nan"))
+    l_p.fill_(float("nan"))
+    dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, num_splits, scale)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    return out, lse
+
+
+@pytest.mark.parametrize("name", ["attn_gqa4_ragged", "attn_gqa8", "attn_mha"])
+@pytest.mark.parametrize("num_splits", [1, 2, 3, 8])
+def test_golden(golden, name, num_splits):
+    g = golden(name)
+    q, k, v, lens = (g[x].cuda() for x in ("q", "k_cache", "v_cache", "cache_seqlens"))
+    out, lse = run(q, k, v, lens, num_splits)
+    assert_attn_close(out, lse, g["out"], g["lse"])
+
+
+def test_config1_contiguous():
+    cfg = configs.ATTN_CONFIG1
+    q, k, v, lens = configs.attn_inputs(cfg)
+    ref_out, ref_lse = oracle.decode_attention(q, k, v, lens)
+    for s in (1, 16, 64):
+        out, lse = run(q, k, v, lens, s)
+        assert_attn_close(out, lse, ref_out, ref_lse)
+
+
+def test_ragged_with_nan_padding_and_edge_lengths():
+    torch.manual_seed(7)
+    B, L, Hq, Hkv = 12, 1000, 16, 4
+    lens = torch.tensor([0, 1, 63, 64, 65, 127, 128, 129, 511, 999, 1000, 333], dtype=torch.int32)
+    q = torch.randn(B, 1, Hq, 128, device="cuda").bfloat16()
+    k = torch.randn(B, L, Hkv, 128, device="cuda").bfloat16()
+    v = torch.randn(B, L, Hkv, 128, device="cuda").bfloat16()
+    for b in range(B):  # padding past each row's length is NaN: it must never leak
+        k[b, lens[b]:] = float("nan")
+        v[b, lens[b]:] = float("nan")
+    lens = lens.cuda()
+    ref_out, ref_lse = oracle.decode_attention(q, k, v, lens)
+    for s in (1, 4, 16):
+        out, lse = run(q, k, v, lens, s)
+        assert torch.isfinite(out.float()).all()
+        assert_attn_close(out, lse, ref_out, ref_lse)
+    assert torch.all(out[0] == 0)
+
+
+def test_lengths_beyond_cache_are_clamped():
+    torch.manual_seed(3)
+    B, L = 3, 200
+    q = torch.randn(B, 1, 8, 128, device="cuda").bfloat16()
+    k = torch.randn(B, L, 2, 128, device="cuda").bfloat16()
+    v = torch.randn(B, L, 2, 128, device="cuda").bfloat16()
+    lens = torch.tensor([500, -4, 150], dtype=torch.int32, device="cuda")
+    ref_out, ref_lse = oracle.decode_attention(q, k, v, lens)
+    out, lse = run(q, k, v, lens, 3)
+    assert_attn_close(out, lse, ref_out, ref_lse)
+
+
+def test_two_pass_api_and_custom_scale():
+    torch.manual_seed(11)
+    B, L, Hq, Hkv = 5, 700, 32, 8
+    q = torch.randn(B, 1, Hq, 128, device="cuda").bfloat16()
+    k = torch.randn(B, L, Hkv, 128, device="cuda").bfloat16()
+    v = torch.randn(B, L, Hkv, 128, device="cuda").bfloat16()
+    lens = torch.tensor([700, 10, 300, 650, 64], dtype=torch.int32, device="cuda")
+    S = 6
+    o_p, l_p = alloc_partials(B, Hq, S, "cuda")
+    out = torch.empty(B, 1, Hq, 128, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, device="cuda")
+    dec_attn_splitkv_partial(q, k, v, lens, o_p, l_p, S, softmax_scale=0.05)
+    dec_attn_combine(o_p, l_p, lens, out, lse, max_seqlen=L)
+    torch.cuda.synchronize()
+    ref_out, ref_lse = oracle.decode_attention(q, k, v, lens, softmax_scale=0.05)
+    assert_attn_close(out, lse, ref_out, ref_lse)
+    # the per-split partials are themselves attention over each split's tokens
+    c = chunk_tokens(L, S)
+    b, s = 3, 2
+    lo, hi = s * c, min((s + 1) * c, int(lens[b]))
+    kk = k[b:b + 1].clone()
+    po, plse = oracle.decode_attention(q[b:b + 1], k[b:b + 1, lo:hi], v[b:b + 1, lo:hi],
+                                       torch.tensor([hi - lo], dtype=torch.int32), softmax_scale=0.05)
+    assert (o_p[s, b].cpu() - po[0]).abs().max().item() < 1e-2
+    assert (l_p[s, b].cpu() - plse[0]).abs().max().item() < LSE_ABS
+    del kk
+
+
+def test_kernel_object_and_stream():
+    torch.manual_seed(5)
+    q = torch.randn(2, 1, 32, 128, device="cuda").bfloat16()
+    k = torch.randn(2, 4096, 8, 128, device="cuda").bfloat16()
+    v = torch.randn(2, 4096, 8, 128, device="cuda").bfloat16()
+    lens = torch.tensor([4096, 1234], dtype=torch.int32, device="cuda")
+    ref_out, ref_lse = oracle.decode_attention(q, k, v, lens)
+    attn = DecodeAttention()
+    out = torch.empty(2, 1, 32, 128, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(2, 32, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        attn(q, k, v, lens, out, lse)
+    s.synchronize()
+    assert_attn_close(out, lse, ref_out, ref_lse)
+    out2, lse2 = decode_attention(q, k, v, lens)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out) or (out2.float() - out.float()).abs().max() < 1e-2
+
+
+def test_deterministic():
+    cfg = configs.ATTN_CONFIG1
+    q, k, v, lens = configs.attn_inputs(cfg)
+    a = run(q, k, v, lens, 16)
+    b = run(q, k, v, lens, 16)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+def test_config2_ragged_full_size():
+    """Full BASELINE size: every row checked against the oracle on a sample of rows."""
+    cfg = configs.ATTN_CONFIG2
+    q, k, v, lens = configs.attn_inputs(cfg)
+    from fused_kernels_cutedsl_lib_b200 import default_num_splits
+
+    S = default_num_splits(cfg.batch, cfg.num_heads_kv, cfg.max_seqlen, int(lens.sum()))
+    out, lse = run(q, k, v, lens, S)
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+    rows = [0, 7, 31, 63] + [int(torch.argmin(lens)), int(torch.argmax(lens))]
+    for r in rows:
+        ro, rl = oracle.decode_attention(q[r:r + 1], k[r:r + 1], v[r:r + 1], lens[r:r + 1])
+        assert_attn_close(out[r:r + 1], lse[r:r + 1], ro, rl)
+    del k, v
+    torch.cuda.empty_cache()
