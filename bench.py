@@ -33,8 +33,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 # DRAM bytes (read + write) per launch of splitkv_fwd_kernel, from the ncu
-# capture summarised in profiles/splitkv_fwd_kernel_config2.md (None until captured).
-NCU_TRAFFIC_BYTES_PER_LAUNCH = None
+# capture summarised in profiles/splitkv_fwd_kernel_config2.md (small case scaled by KV bytes).
+NCU_TRAFFIC_BYTES_PER_LAUNCH = 4_615_000_000  # 542.3 MB at 537 MB of KV, scaled x8.51
 
 
 def _peaks():
@@ -46,47 +46,79 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms around the timed region.
+
+    A reader thread timestamps every sample; ``mark_start``/``mark_end`` bracket
+    the timed region and only samples inside it are summarised (the sample
+    nearest the region is used if the region is shorter than the period).
+    """
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, device_index: int):
+        import threading
+
+        self.samples: list[tuple[float, list[str]]] = []
         self.proc = None
+        self.t0 = self.t1 = None
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
         try:
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+                ["nvidia-smi", "-i", bus, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+        except Exception as e:  # no nvidia-smi: report no clocks
+            self.error = repr(e)
+            return
+        self.error = None
+        self.first = threading.Event()
+
+        def reader():
+            for line in self.proc.stdout:
+                self.samples.append((time.perf_counter(), [x.strip() for x in line.split(",")]))
+                self.first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        self.first.wait(timeout=5)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+        if self.proc is not None:
+            time.sleep(0.15)  # let the sample covering the end arrive
 
     def stop(self) -> dict | None:
         if self.proc is None:
-            return None
+            return {"error": self.error}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+        good = [(t, f) for t, f in self.samples if len(f) >= 8]
+        if not good:
+            return {"error": "no samples: " + " | ".join(",".join(f) for _, f in self.samples[:2])}
+        inside = [f for t, f in good if self.t0 is not None and self.t0 <= t <= (self.t1 or t) + 0.1]
+        if not inside and self.t0 is not None:
+            inside = [min(good, key=lambda tf: abs(tf[0] - self.t0))[1]]
         sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 8:
-                continue
+        for f in inside:
             try:
                 sms.append(float(f[0]))
                 maxes.append(float(f[1]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[4:8]):
+            for n, v in zip(self.NAMES, f[4:8]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sms:
-            return None
+            return {"error": "unparsable samples"}
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
                 "samples": len(sms)}
 
@@ -145,6 +177,7 @@ def run_ours(args):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     from fused_kernels_cutedsl_lib_b200.decoding_attention import dec_attn_combine, dec_attn_splitkv_partial
+    clocks.mark_start()
     t_start.record(stream)
     for i in range(args.steps):
         e0, e1, e2 = evs[i]
@@ -155,6 +188,7 @@ def run_ours(args):
         e2.record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
+    clocks.mark_end()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
@@ -322,7 +356,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

@@ -1,0 +1,52 @@
+"""Small, fixed workloads for Nsight Compute captures of single kernels.
+
+Each case builds its inputs (larger than the 126 MB L2 so DRAM counters are
+meaningful, a few GB at most), runs a few warm-up launches and then
+``--launches`` launches of one kernel, and exits. The profiles/ summaries name
+the exact command, e.g.
+
+    ncu --set full --clock-control none -k regex:splitkv_fwd -s 2 -c 1 \
+        python -m fused_kernels_cutedsl_lib_b200.profile_cases attn_small
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+
+def case_attn_small(launches: int):
+    """Decode attention B=16, 32q/8kv, every row at 8192 tokens: 537 MB of KV per launch."""
+    from . import alloc_partials, dec_attn_splitkv_fwd, default_num_splits
+
+    B, L, Hq, Hkv = 16, 8192, 32, 8
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, 1, Hq, 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, L, Hkv, 128, device="cuda", generator=g, dtype=torch.bfloat16)
+    v = torch.randn(B, L, Hkv, 128, device="cuda", generator=g, dtype=torch.bfloat16)
+    lens = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    S = default_num_splits(B, Hkv, L)
+    out = torch.empty(B, 1, Hq, 128, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, device="cuda")
+    o_p, l_p = alloc_partials(B, Hq, S, "cuda")
+    for _ in range(2 + launches):
+        dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, S)
+    torch.cuda.synchronize()
+    print(f"attn_small: B={B} L={L} splits={S} kv_bytes={B * L * Hkv * 128 * 4}")
+
+
+CASES = {
+    "attn_small": case_attn_small,
+}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--launches", type=int, default=3)
+    args = ap.parse_args()
+    CASES[args.case](args.launches)
+
+
+if __name__ == "__main__":
+    main()
