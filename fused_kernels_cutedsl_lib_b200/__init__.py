@@ -4,6 +4,20 @@ Host code is Python/PyTorch over the C ABI of ``_lib/libfk_b200.so``
 (``include/fk_b200.h``); the kernels are hand-written CUDA for sm_100a. There is
 no CPU or eager fallback: if the library is missing, calls raise.
 """
+from .cdsl_fn_utils import compile_cutedsl
+from .gemm import (
+    Gemm4SM90,
+    RMSNormLinear1SM90,
+    Swiglu2SM90,
+    SwigluSM90,
+    alloc_workspace,
+    linear,
+    rmsnorm_linear,
+    skinny_gemm,
+    swiglu_gemm,
+    swiglu_gemm2,
+    workspace_bytes,
+)
 from .decoding_attention import (
     DecodeAttention,
     alloc_partials,
@@ -16,6 +30,18 @@ from .decoding_attention import (
 )
 
 __all__ = [
+    "Gemm4SM90",
+    "RMSNormLinear1SM90",
+    "Swiglu2SM90",
+    "SwigluSM90",
+    "alloc_workspace",
+    "compile_cutedsl",
+    "linear",
+    "rmsnorm_linear",
+    "skinny_gemm",
+    "swiglu_gemm",
+    "swiglu_gemm2",
+    "workspace_bytes",
     "DecodeAttention",
     "alloc_partials",
     "chunk_tokens",

@@ -37,6 +37,18 @@ SIGNATURES: dict[str, tuple] = {
         [_p, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
          _c_float, _p],
     ),
+    "fk_linear_workspace_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(ctypes.c_size_t)]),
+    "fk_linear": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p],
+    ),
+    "fk_skinny_gemm": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
+    "fk_rmsnorm_linear": (
+        _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
+    "fk_swiglu_gemm": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
+    "fk_swiglu_gemm2": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
+    "fk_rmsnorm_swiglu": (
+        _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
 }
 
 _lock = threading.Lock()

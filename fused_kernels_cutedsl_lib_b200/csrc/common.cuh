@@ -65,10 +65,15 @@ enum DeviceError : int {
   kDevErrFlagWait = 4,    // waited too long on a global flag
 };
 
-// Bound on mbarrier polls. Each try_wait already suspends for a
-// hardware-chosen interval, so 1<<24 polls is several seconds: far above any
-// legitimate wait, far below a watchdog.
-constexpr uint32_t kMaxPolls = 1u << 24;
+// Bound on any single wait, in nanoseconds of %globaltimer: far above any
+// legitimate wait inside these kernels (microseconds), far below a watchdog.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -109,8 +114,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete.
 // Returns false (and records `err`) when the bound runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) break;
   }
   record_device_error(err, code);
   return false;

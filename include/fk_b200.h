@@ -21,6 +21,7 @@
 #ifndef FK_B200_H_
 #define FK_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -95,6 +96,57 @@ FK_API int fk_dec_attn_fwd(const void* q, const void* k_cache, const void* v_cac
                     float* lse_partial, int batch, int max_seqlen, int num_heads_q,
                     int num_heads_kv, int head_dim, int num_splits, float softmax_scale,
                     void* stream);
+
+/* ---- linear family: y[M, N] = epilogue(x[M, K] . W[N, K]^T) ---------------
+ * x bf16 [M, K] (K % 8 == 0, 16-byte aligned), W bf16 [N, K] (row = output
+ * feature), y bf16 [M, N], fp32 accumulation. M <= 16 runs the persistent
+ * stream-K weight-streaming kernel (mma.sync, W as the M side); M > 16 runs
+ * the tcgen05/TMEM kernel (token tiles of up to 256).
+ *
+ * `workspace` is caller scratch for the stream-K split partials and per-row-
+ * block counters: at least fk_linear_workspace_bytes(...) bytes, 256-byte
+ * aligned, ZERO-FILLED before its first use. Every call leaves the counters
+ * at zero again, so one workspace serves any number of calls in stream
+ * order; calls that overlap on the GPU need separate workspaces.
+ */
+#define FK_LINEAR_SWIGLU 1
+
+FK_API int fk_linear_workspace_bytes(int M, int N, int K, int flags, size_t* bytes_out);
+
+/* General form. gamma (bf16 [K]) non-null => RMSNorm of x (with eps) fused in;
+ * w_up non-null => SwiGLU: y = silu(x.W[n]) * (x.W_up[up_row_offset + n]);
+ * residual (bf16 [M, N]) non-null => added in the epilogue (may alias y). */
+FK_API int fk_linear(const void* x, const void* gamma, const void* w, const void* w_up,
+                     int up_row_offset, const void* residual, void* y, int M, int N, int K,
+                     float eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* y = x W^T. Replaces Gemm4SM90(...)(a, b, c)
+ * (python/cutedsl_kernels/gemm/kernel/attempt4.py:133-168; check demo/gemm_run.py:29). */
+FK_API int fk_skinny_gemm(const void* x, const void* w, void* y, int M, int N, int K,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* y = rms_norm(x, gamma, eps) W^T. Replaces RMSNormLinear1SM90(...)(a, b, c, stream)
+ * (python/cutedsl_kernels/rmsnorm_linear/attempt1/gemm.py:136-170, check :721-722),
+ * adding the gain gamma. */
+FK_API int fk_rmsnorm_linear(const void* x, const void* gamma, const void* w, void* y, int M,
+                             int N, int K, float eps, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* y[M, N] = silu(x Wg^T) * (x Wu^T) with w_gate_up = [Wg; Wu] of shape [2N, K]
+ * (demo/swiglu.py:47-49 `(a @ bb1.t()).chunk(2)`). */
+FK_API int fk_swiglu_gemm(const void* x, const void* w_gate_up, void* y, int M, int N, int K,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Two-weight form: replaces Swiglu2SM90(...)(a, b, b1, c)
+ * (python/cutedsl_kernels/swiglu/attempt1/gemm2.py:145-187, check :714-717). */
+FK_API int fk_swiglu_gemm2(const void* x, const void* w_gate, const void* w_up, void* y, int M,
+                           int N, int K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* RMSNorm -> gate/up projection -> SwiGLU in one kernel (the FFN input of the
+ * decode layer). */
+FK_API int fk_rmsnorm_swiglu(const void* x, const void* gamma, const void* w_gate_up, void* y,
+                             int M, int N, int K, float eps, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

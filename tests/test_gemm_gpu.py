@@ -1,0 +1,191 @@
+"""Parity of the linear family (skinny stream-K and tcgen05 kernels) against the CPU oracle (GPU)."""
+import pytest
+import torch
+
+import oracle
+from fused_kernels_cutedsl_lib_b200 import (
+    Gemm4SM90,
+    RMSNormLinear1SM90,
+    Swiglu2SM90,
+    _native,
+    alloc_workspace,
+    compile_cutedsl,
+    linear,
+    rmsnorm_linear,
+    skinny_gemm,
+    swiglu_gemm,
+    swiglu_gemm2,
+    workspace_bytes,
+)
+from fused_kernels_cutedsl_lib_b200 import configs
+
+pytestmark = pytest.mark.gpu
+
+# bf16 outputs vs an fp32 reference. Scaled error |out - ref| / max(1, |ref|):
+# the output's own bf16 rounding is 2^-9 relative, so an absolute bound cannot
+# hold for |ref| > 8 (SwiGLU products reach tens).
+MAX_ERR = 2e-2
+MEAN_ERR = 2e-3
+
+
+def assert_close(out, ref):
+    out = out.float().cpu()
+    ref = ref.float()
+    assert out.shape == ref.shape
+    assert torch.isfinite(out).all()
+    e = (out - ref).abs() / ref.abs().clamp_min(1.0)
+    assert e.max().item() <= MAX_ERR, f"max scaled err {e.max().item():.3e}"
+    assert e.mean().item() <= MEAN_ERR, f"mean scaled err {e.mean().item():.3e}"
+
+
+def mk(M, N, K, seed=0, w_std=0.02):
+    return configs.gemm_inputs(M, N, K, seed, w_std=w_std)
+
+
+def gamma_of(K, seed=9):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).bfloat16()
+
+
+def finish():
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+
+
+def test_golden_fixtures(golden):
+    g = golden("skinny_gemm")
+    y = skinny_gemm(g["x"].cuda(), g["w"].cuda())
+    finish()
+    assert_close(y, g["y"])
+    g = golden("swiglu")
+    y = swiglu_gemm(g["x"].cuda(), g["w_gate_up"].cuda())
+    finish()
+    assert_close(y, g["y"])
+    g = golden("swiglu_two_weights")
+    y = swiglu_gemm2(g["x"].cuda(), g["b"].cuda(), g["b1"].cuda())
+    finish()
+    assert_close(y, g["y"])
+    g = golden("rmsnorm_linear")
+    x = g["x"].cuda()
+    y = rmsnorm_linear(x, torch.ones(x.shape[1], dtype=torch.bfloat16, device="cuda"), g["w"].cuda(), eps=g["eps"])
+    finish()
+    assert_close(y, g["y"])
+
+
+SKINNY_M = [1, 2, 4, 8, 9, 16]
+TC_M = [17, 32, 64, 100, 128, 256]
+
+
+@pytest.mark.parametrize("M", SKINNY_M + TC_M)
+def test_plain_config3_shape(M):
+    x, w = mk(M, 14336, 4096, seed=2)
+    y = torch.full((M, 14336), float("nan"), dtype=torch.bfloat16, device="cuda")
+    skinny_gemm(x, w, y)
+    finish()
+    assert_close(y, oracle.linear(x, w))
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 40, 128])
+@pytest.mark.parametrize("N,K", [(200, 136), (1000, 520), (6144, 4096), (4096, 14336)])
+def test_plain_ragged_shapes(M, N, K):
+    x, w = mk(M, N, K, seed=M + N)
+    y = skinny_gemm(x, w)
+    finish()
+    assert_close(y, oracle.linear(x, w))
+
+
+@pytest.mark.parametrize("M", [1, 16, 128])
+def test_rmsnorm_linear_config4(M):
+    x, w = mk(M, 6144, 4096, seed=3)
+    gam = gamma_of(4096)
+    y = rmsnorm_linear(x, gam, w, eps=1e-6)
+    finish()
+    assert_close(y, oracle.rmsnorm_linear(x, gam, w, eps=1e-6))
+
+
+@pytest.mark.parametrize("M", [1, 16, 128])
+def test_swiglu_config4(M):
+    x, w = mk(M, 2 * 14336, 4096, seed=3)
+    y = swiglu_gemm(x, w)
+    finish()
+    assert_close(y, oracle.swiglu(x, w))
+
+
+@pytest.mark.parametrize("M", [3, 16, 64, 200])
+def test_rmsnorm_swiglu_and_two_weight_forms(M):
+    x, w = mk(M, 2 * 1536, 2048, seed=M)
+    gam = gamma_of(2048)
+    y = swiglu_gemm(x, w, gamma=gam, eps=1e-5)
+    finish()
+    ref = oracle.swiglu(oracle.rmsnorm(x, gam, 1e-5), w)
+    assert_close(y, ref)
+    y2 = swiglu_gemm2(x, w[:1536].contiguous(), w[1536:].contiguous())
+    finish()
+    assert_close(y2, oracle.swiglu(x, w))
+
+
+@pytest.mark.parametrize("M", [1, 16, 48, 300])
+def test_residual_epilogue_in_place(M):
+    x, w = mk(M, 4096, 4096, seed=5)
+    res = torch.randn(M, 4096, device="cuda").bfloat16()
+    ref = oracle.linear(x, w) + res.float().cpu()
+    out = res.clone()
+    linear(x, w, out, residual=out)  # y = residual + x W^T, written over the residual
+    finish()
+    assert_close(out, ref)
+
+
+def test_deterministic_and_workspace_reuse():
+    x, w = mk(8, 14336, 4096, seed=1)
+    a = skinny_gemm(x, w)
+    b = skinny_gemm(x, w)
+    x2, w2 = mk(128, 14336, 4096, seed=1)
+    c = skinny_gemm(x2, w2)
+    d = skinny_gemm(x2, w2)
+    finish()
+    assert torch.equal(a, b) and torch.equal(c, d)
+
+
+def test_explicit_workspace_and_stream():
+    x, w = mk(16, 6144, 4096, seed=4)
+    nb = workspace_bytes(16, 6144, 4096)
+    ws = alloc_workspace(nb, "cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        y = skinny_gemm(x, w, workspace=ws)
+    s.synchronize()
+    finish()
+    assert_close(y, oracle.linear(x, w))
+    assert int(ws[:4 * 48].view(torch.int32).abs().sum()) == 0  # counters back at zero
+
+
+def test_reference_style_kernel_objects():
+    x, w = mk(16, 4096, 4096, seed=6)
+    c = torch.empty(16, 4096, dtype=torch.bfloat16, device="cuda")
+    k = Gemm4SM90(tile_shape_mnk=(128, 256, 32), epi_tile_mn=(128, 128), cluster_shape_mnk=(2, 1, 1),
+                  atom_layout_mn=(2, 1), ab_stage=6, epi_stage=2, is_persistent=True, gemm_n_prologue=1)
+    f = compile_cutedsl((x, w, c), k, False)
+    f(x, w, c)
+    finish()
+    assert_close(c, oracle.linear(x, w))
+    r = RMSNormLinear1SM90(eps=1e-5)
+    r(x, w, c, torch.cuda.current_stream())
+    finish()
+    assert_close(c, oracle.rmsnorm_linear(x, None, w, eps=1e-5))
+    b1 = mk(16, 4096, 4096, seed=7)[1]
+    Swiglu2SM90(tile_shape_mnk=(128, 128, 32))(x, w, b1, c)
+    finish()
+    assert_close(c, oracle.swiglu_separate(x, w, b1))
+
+
+def test_bad_arguments_raise():
+    x, w = mk(4, 256, 256)
+    with pytest.raises(TypeError):
+        skinny_gemm(x.float(), w)
+    with pytest.raises(ValueError):
+        skinny_gemm(x[:, :128], w)
+    with pytest.raises(ValueError):
+        skinny_gemm(x, w, torch.empty(4, 100, dtype=torch.bfloat16, device="cuda"))
+    x9 = torch.zeros(4, 260, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        skinny_gemm(x9, torch.zeros(8, 260, dtype=torch.bfloat16, device="cuda"))
