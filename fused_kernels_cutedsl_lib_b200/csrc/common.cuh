@@ -50,6 +50,13 @@ int encode_tma(CUtensorMap* map, CUtensorMapDataType dtype, int rank,
                const uint32_t* box, CUtensorMapSwizzle swizzle,
                CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 
+// Stream-K workspace header: a fixed block of per-row-block counters at the
+// start of every linear-family workspace, whatever the call's shape, so that
+// fp32 partials of one call can never land on the counters of another call
+// sharing the workspace. Supports up to kMaxRowBlocks row blocks (N <= 512K).
+constexpr int kMaxRowBlocks = 4096;
+constexpr size_t kCounterBytes = kMaxRowBlocks * sizeof(int);  // 16 KB
+
 // Device address of this library's error word on the current device (set up
 // once per device). Kernels take it as `int* err`.
 int* device_error_word();

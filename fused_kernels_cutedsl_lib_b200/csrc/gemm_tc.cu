@@ -452,8 +452,8 @@ static int token_tile(int M) { return M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 1
 size_t tc_workspace_bytes(int M, int N, int K, bool swiglu) {
   (void)K;
   const int num_rb = (N + tc::BM - 1) / tc::BM;
-  const size_t cnt = ((size_t)num_rb * 4 + 255) / 256 * 256;
-  return cnt + (size_t)2 * num_sms() * tc::slot_floats(tc::token_tile(M), swiglu) * 4;
+  (void)num_rb;
+  return kCounterBytes + (size_t)2 * num_sms() * tc::slot_floats(tc::token_tile(M), swiglu) * 4;
 }
 
 int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
@@ -462,6 +462,7 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   FK_CHECK_ARG(x && w && y, "null tensor pointer");
   FK_CHECK_ARG(M >= 1 && N >= 1 && K >= 1, "sizes must be positive");
   FK_CHECK_ARG(K % 8 == 0, "K must be a multiple of 8 (16-byte rows for TMA)");
+  FK_CHECK_ARG((N + 127) / 128 <= kMaxRowBlocks, "N too large: at most 4096 row blocks of 128");
   FK_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 && (!w_up || ((uintptr_t)w_up & 15) == 0) &&
                    (!gamma || ((uintptr_t)gamma & 15) == 0),
                "x, w, gamma must be 16-byte aligned");
@@ -477,7 +478,7 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   tc::Params p;
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.counters = static_cast<int*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t)num_rb * 4 + 255) / 256 * 256);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
   p.err = err;
   p.N = N;
   p.K = K;

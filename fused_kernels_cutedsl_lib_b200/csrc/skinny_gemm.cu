@@ -403,8 +403,8 @@ static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtenso
 // Workspace layout shared by the skinny path: [counters: num_rb ints, 256-B aligned][partials].
 size_t skinny_workspace_bytes(int N, int G, bool swiglu) {
   const int num_rb = (N + sk::RB - 1) / sk::RB;
-  const size_t cnt = ((size_t)num_rb * 4 + 255) / 256 * 256;
-  return cnt + (size_t)2 * G * sk::slot_floats(swiglu) * 4;
+  (void)num_rb;
+  return kCounterBytes + (size_t)2 * G * sk::slot_floats(swiglu) * 4;
 }
 
 // Shared entry used by every skinny-path C function. `w_up` null => no SwiGLU.
@@ -415,6 +415,7 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   FK_CHECK_ARG(M >= 1 && M <= sk::MAXM, "skinny path takes 1 <= M <= 16");
   FK_CHECK_ARG(N >= 1 && K >= 1, "N and K must be positive");
   FK_CHECK_ARG(K % 8 == 0, "K must be a multiple of 8 (16-byte rows for TMA)");
+  FK_CHECK_ARG((N + 127) / 128 <= kMaxRowBlocks, "N too large: at most 4096 row blocks of 128");
   FK_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 && (!w_up || ((uintptr_t)w_up & 15) == 0) &&
                    (!gamma || ((uintptr_t)gamma & 15) == 0),
                "x, w, gamma must be 16-byte aligned");
@@ -434,7 +435,7 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   p.y = static_cast<__nv_bfloat16*>(y);
   p.counters = static_cast<int*>(workspace);
   const int num_rb = (N + sk::RB - 1) / sk::RB;
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t)num_rb * 4 + 255) / 256 * 256);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
   p.err = err;
   p.M = M;
   p.N = N;

@@ -189,3 +189,17 @@ def test_bad_arguments_raise():
     x9 = torch.zeros(4, 260, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):
         skinny_gemm(x9, torch.zeros(8, 260, dtype=torch.bfloat16, device="cuda"))
+
+
+def test_shared_workspace_across_shapes():
+    """One workspace reused by calls of very different N and M (stale partials must never act as counters)."""
+    ws = alloc_workspace(max(workspace_bytes(16, 14336, 4096, True), workspace_bytes(256, 14336, 4096, True)), "cuda")
+    shapes = [(1, 256, 4096), (1, 1024, 256), (1, 14336, 256), (5, 96, 256), (16, 14336, 4096),
+              (64, 640, 512), (128, 14336, 256), (3, 14336, 4096)]
+    for rep in range(2):
+        for (M, N, K) in shapes:
+            x, w = mk(M, N, K, seed=M * 7 + N + rep)
+            y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+            skinny_gemm(x, w, y, workspace=ws)
+            finish()
+            assert_close(y, oracle.linear(x, w))
