@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
       const int col = rb * BM + row;
       if (full_rb) {
-        for (int c0 = 0; c0 < NMMA; c0 += 16) {
+        for (int c0 = 0; c0 < NMMA && c0 < p.M; c0 += 16) {
           float a[16], u[16];
           tmem_ld16(trow + c0, a);
           if (SWIGLU) tmem_ld16(trow + NMMA + c0, u);
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       } else {
         const int slot = 2 * cta + (seg_lo == it_begin ? 0 : 1);
         float* sp = p.partials + (size_t)slot * SLOT;
-        for (int c0 = 0; c0 < NMMA; c0 += 16) {
+        for (int c0 = 0; c0 < NMMA && c0 < p.M; c0 += 16) {
           float a[16];
           tmem_ld16(trow + c0, a);
 #pragma unroll
@@ -387,22 +387,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             named_bar_sync(1, EPI_THREADS);
           }
-          for (int m = 0; m < NMMA && m < p.M; ++m) {
-            float g = 0.f, u = 0.f;
+          // Sum the contributors' partials 16 tokens at a time: 16 (or 32)
+          // independent loads in flight per contributor keep this
+          // throughput-bound instead of latency-bound.
+          for (int c0 = 0; c0 < NMMA && c0 < p.M; c0 += 16) {
+            float g[16], u[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) g[i] = u[i] = 0.f;
             for (int cc = cf; cc < p.G && it_start(p, cc) < hi; ++cc) {
               if (it_start(p, cc + 1) == it_start(p, cc)) continue;
               const int sl = 2 * cc + (it_start(p, cc) >= lo ? 0 : 1);
-              const float* qp = p.partials + (size_t)sl * SLOT;
-              g += __ldcg(qp + (size_t)m * BM + row);
-              if (SWIGLU) u += __ldcg(qp + (size_t)NMMA * BM + (size_t)m * BM + row);
+              const float* qp = p.partials + (size_t)sl * SLOT + (size_t)c0 * BM + row;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) g[i] += __ldcg(qp + i * BM);
+              if (SWIGLU) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) u[i] += __ldcg(qp + (size_t)NMMA * BM + i * BM);
+              }
             }
             if (col < p.N) {
-              float rs = 1.f;
-              if (NORM) rs = rsqrtf(ss_sm[m] * p.inv_k + p.eps);
-              float val = SWIGLU ? silu_f(g * rs) * (u * rs) : g * rs;
-              const size_t off = (size_t)m * p.N + col;
-              if (p.residual) val += __bfloat162float(p.residual[off]);
-              p.y[off] = __float2bfloat16_rn(val);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int m = c0 + i;
+                if (m < p.M) {
+                  float rs = 1.f;
+                  if (NORM) rs = rsqrtf(ss_sm[m] * p.inv_k + p.eps);
+                  float val = SWIGLU ? silu_f(g[i] * rs) * (u[i] * rs) : g[i] * rs;
+                  const size_t off = (size_t)m * p.N + col;
+                  if (p.residual) val += __bfloat162float(p.residual[off]);
+                  p.y[off] = __float2bfloat16_rn(val);
+                }
+              }
             }
           }
         }

@@ -1,0 +1,136 @@
+"""Timing helpers and the GEMM-family sweep (configs 3 and 4).
+
+Every single-kernel number is the median of CUDA-event timings of individual
+launches on the launching stream. The weights of these configs (50-235 MB)
+would otherwise sit partly in the 126 MB L2 between iterations, so each case
+keeps several copies of its weight (together > 300 MB) and launch i reads copy
+i mod n: every launch streams its weight from HBM. (A flush by writing a large
+buffer would leave L2 full of dirty lines whose write-back lands inside the
+next timed launch.) Algorithmic bytes per call =
+weights + x + y (+ gamma); FLOPs = 2·M·N·K (x2 for SwiGLU's two products).
+"""
+from __future__ import annotations
+
+import json
+import statistics
+from pathlib import Path
+
+import torch
+
+from . import configs
+from .gemm import linear, workspace_bytes, alloc_workspace
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "kind": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "kind": "fallback"}
+
+
+class L2Flusher:
+    def __init__(self, nbytes: int = 512 << 20, device="cuda"):
+        self.buf = torch.empty(nbytes // 4, dtype=torch.int32, device=device)
+
+    def __call__(self):
+        self.buf.fill_(0)
+
+
+def time_launches(fn, iters: int = 30, warmup: int = 3, flush: L2Flusher | None = None) -> list[float]:
+    """Per-launch device times (ms) from CUDA events on the current stream; ``fn(i)``."""
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    times = []
+    for i in range(iters):
+        if flush is not None:
+            flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn(i)
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return times
+
+
+def weight_copies(w: torch.Tensor, min_total: int = 320 << 20) -> list[torch.Tensor]:
+    """``w`` plus clones so that the copies together exceed ``min_total`` bytes (>= 2 copies)."""
+    nb = w.numel() * w.element_size()
+    n = max(2, -(-min_total // nb) + 1)
+    return [w] + [w.clone() for _ in range(n - 1)]
+
+
+def gemm_sweep(iters: int = 30, include_cublas: bool = True) -> list[dict]:
+    """Config 3 (skinny GEMM, M sweep) and config 4 (RMSNorm->QKV, SwiGLU) on this GPU."""
+    peaks = measured_peaks()
+    rows = []
+    cases = [("skinny_gemm", m, 14336, 4096, 2) for m in (1, 4, 8, 16, 64, 256)]
+    cases += [("rmsnorm_qkv", m, 6144, 4096, 3) for m in (1, 16, 128)]
+    cases += [("swiglu_gate_up", m, 14336, 4096, 3) for m in (1, 16, 128)]
+    for kind, M, N, K, seed in cases:
+        rows_w = 2 * N if kind == "swiglu_gate_up" else N
+        x, w = configs.gemm_inputs(M, rows_w, K, seed)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        gamma = None
+        if kind == "rmsnorm_qkv":
+            g = torch.Generator(device="cuda").manual_seed(seed)
+            gamma = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).bfloat16()
+        sw = kind == "swiglu_gate_up"
+        ws = alloc_workspace(workspace_bytes(M, N, K, sw), "cuda")
+
+        ws_list = weight_copies(w)
+        nw = len(ws_list)
+
+        def ours(i):
+            wi = ws_list[i % nw]
+            if sw:
+                linear(x, wi, y, w_up=wi, up_row_offset=N, workspace=ws)
+            else:
+                linear(x, wi, y, gamma=gamma, eps=1e-6, workspace=ws)
+
+        t = statistics.median(time_launches(ours, iters))
+        nbytes = rows_w * K * 2 + M * K * 2 + M * N * 2 + (K * 2 if gamma is not None else 0)
+        flops = 2 * M * rows_w * K
+        row = {"kernel": kind, "M": M, "N": N, "K": K, "us": round(t * 1e3, 2),
+               "TBps": round(nbytes / (t * 1e-3) / 1e12, 3),
+               "hbm_frac": round(nbytes / (t * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
+               "TFLOPs": round(flops / (t * 1e-3) / 1e12, 1),
+               "path": "stream-K mma.sync" if M <= 16 else "tcgen05/TMEM"}
+        if include_cublas:
+            if sw:
+                def ref(i):
+                    o = x @ ws_list[i % nw].t()
+                    torch.nn.functional.silu(o[:, :N]) * o[:, N:]
+            elif gamma is not None:
+                def ref(i):
+                    torch.nn.functional.rms_norm(x, (K,), weight=gamma, eps=1e-6) @ ws_list[i % nw].t()
+            else:
+                def ref(i):
+                    x @ ws_list[i % nw].t()
+            tr = statistics.median(time_launches(ref, iters))
+            row["torch_us"] = round(tr * 1e3, 2)
+            row["speedup_vs_torch"] = round(tr / t, 2)
+        row["weight_copies"] = nw
+        rows.append(row)
+        del x, w, y, ws, ws_list
+    return rows
+
+
+def main():
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=30)
+    args = ap.parse_args()
+    for r in gemm_sweep(args.iters):
+        print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

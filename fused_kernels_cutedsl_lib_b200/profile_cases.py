@@ -35,8 +35,52 @@ def case_attn_small(launches: int):
     print(f"attn_small: B={B} L={L} splits={S} kv_bytes={B * L * Hkv * 128 * 4}")
 
 
+def _gemm_case(M, N, K, launches, kind="plain"):
+    from . import configs
+    from .gemm import alloc_workspace, linear, workspace_bytes
+
+    rows = 2 * N if kind == "swiglu" else N
+    x, w = configs.gemm_inputs(M, rows, K, 2)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    gamma = torch.ones(K, dtype=torch.bfloat16, device="cuda") if kind == "rms" else None
+    ws = alloc_workspace(workspace_bytes(M, N, K, kind == "swiglu"), "cuda")
+    flush = torch.empty(256 << 18, dtype=torch.int32, device="cuda")  # 256 MB L2 flush
+    for _ in range(2 + launches):
+        flush.fill_(0)
+        if kind == "swiglu":
+            linear(x, w, y, w_up=w, up_row_offset=N, workspace=ws)
+        else:
+            linear(x, w, y, gamma=gamma, workspace=ws)
+    torch.cuda.synchronize()
+    print(f"gemm {kind}: M={M} N={N} K={K} weight_bytes={rows * K * 2}")
+
+
+def case_skinny_m16(launches: int):
+    """Skinny stream-K GEMM, config 3 at M=16: W [14336, 4096] = 117 MB."""
+    _gemm_case(16, 14336, 4096, launches)
+
+
+def case_skinny_m1(launches: int):
+    """Skinny stream-K GEMM, config 3 at M=1."""
+    _gemm_case(1, 14336, 4096, launches)
+
+
+def case_tc_m256(launches: int):
+    """tcgen05 GEMM, config 3 at M=256."""
+    _gemm_case(256, 14336, 4096, launches)
+
+
+def case_tc_m128_swiglu(launches: int):
+    """tcgen05 SwiGLU gate/up GEMM, config 4 at M=128: W [28672, 4096] = 235 MB."""
+    _gemm_case(128, 14336, 4096, launches, "swiglu")
+
+
 CASES = {
     "attn_small": case_attn_small,
+    "skinny_m16": case_skinny_m16,
+    "skinny_m1": case_skinny_m1,
+    "tc_m256": case_tc_m256,
+    "tc_m128_swiglu": case_tc_m128_swiglu,
 }
 
 
