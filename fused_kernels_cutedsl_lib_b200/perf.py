@@ -39,8 +39,14 @@ class L2Flusher:
         self.buf.fill_(0)
 
 
-def time_launches(fn, iters: int = 30, warmup: int = 3, flush: L2Flusher | None = None) -> list[float]:
-    """Per-launch device times (ms) from CUDA events on the current stream; ``fn(i)``."""
+def time_launches(fn, iters: int = 30, warmup: int = 3, flush: L2Flusher | None = None,
+                  busy_cycles: int = 400_000) -> list[float]:
+    """Per-launch device times (ms) from CUDA events on the current stream; ``fn(i)``.
+
+    A ~0.2 ms device spin is queued ahead of each timed launch so the host's
+    enqueue work (argument checks, TMA descriptor encoding) happens while the
+    GPU is busy and never shows up between the two events.
+    """
     stream = torch.cuda.current_stream()
     for i in range(warmup):
         fn(i)
@@ -49,6 +55,7 @@ def time_launches(fn, iters: int = 30, warmup: int = 3, flush: L2Flusher | None 
     for i in range(iters):
         if flush is not None:
             flush()
+        torch.cuda._sleep(busy_cycles)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
