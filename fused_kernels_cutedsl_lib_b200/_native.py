@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple] = {
         _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
     "fk_swiglu_gemm": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
     "fk_swiglu_gemm2": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
+    "fk_skinny_gemm_noalloc": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p]),
     "fk_rmsnorm_swiglu": (
         _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
 }

@@ -148,6 +148,17 @@ FK_API int fk_rmsnorm_swiglu(const void* x, const void* gamma, const void* w_gat
                              int M, int N, int K, float eps, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Skinny GEMM y = x W^T (1 <= M <= 16, N <= 524288) that allocates nothing:
+ * its stream-K scratch is a fixed ~2.7 MB device array inside this library
+ * (one per GPU, kept until process exit) instead of a caller workspace. For
+ * callers that cannot allocate GPU memory while they run (a runtime that owns
+ * every allocation, plain-C callers without an allocator). No counterpart in
+ * the reference. The first call on a device looks up the array's address; make
+ * it before any stream capture. All calls share the array: calls that may
+ * overlap on the GPU race, so order them on one stream. */
+FK_API int fk_skinny_gemm_noalloc(const void* x, const void* w, void* y, int M, int N, int K,
+                                  void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
