@@ -48,6 +48,15 @@ SIGNATURES: dict[str, tuple] = {
     "fk_swiglu_gemm": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
     "fk_swiglu_gemm2": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p]),
     "fk_skinny_gemm_noalloc": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p]),
+    "fk_dec_attn_fwd_ex": (
+        _c_int,
+        [_p, ctypes.c_longlong, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_float, _p],
+    ),
+    "fk_kv_append": (
+        _c_int,
+        [_p, ctypes.c_longlong, _c_int, _c_int, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p],
+    ),
     "fk_rmsnorm_swiglu": (
         _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
 }

@@ -39,7 +39,8 @@ constexpr int TILE_BYTES = 2 * HALF_BYTES; // K (or V) tile: 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;// K + V: 32 KB
 
 struct Params {
-  const __nv_bfloat16* q;  // [B, Hq, D]
+  const __nv_bfloat16* q;  // row b at q + b * q_stride: [Hq, D] contiguous
+  long long q_stride;      // elements between batch rows of q (Hq * D when dense)
   const int* seqlens;      // [B]
   float* o_part;           // [S, B, Hq, D]
   float* lse_part;         // [S, B, Hq]
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // Q^T as the B operand: column n = query head g of the group (zero if g >= G).
     uint32_t qf[8][2];
     {
-      const __nv_bfloat16* qrow = p.q + ((size_t)b * p.Hq + (size_t)h * G + g) * D;
+      const __nv_bfloat16* qrow = p.q + (size_t)b * p.q_stride + ((size_t)h * G + g) * D;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         if (g < G) {
@@ -423,10 +424,12 @@ int fk_dec_attn_chunk_tokens(int max_seqlen, int num_splits) {
   return attn::chunk_tokens(max_seqlen, num_splits);
 }
 
-int fk_dec_attn_splitkv_fwd(const void* q, const void* k_cache, const void* v_cache,
+static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cache, const void* v_cache,
                             const int32_t* cache_seqlens, float* o_partial, float* lse_partial,
                             int batch, int max_seqlen, int num_heads_q, int num_heads_kv,
                             int head_dim, int num_splits, float softmax_scale, void* stream) {
+  FK_CHECK_ARG(q_stride >= (long long)num_heads_q * head_dim && q_stride % 8 == 0,
+               "q row stride must be >= num_heads_q * head_dim and a multiple of 8");
   int rc = check_attn_args(q, k_cache, v_cache, cache_seqlens, batch, max_seqlen, num_heads_q,
                            num_heads_kv, head_dim, num_splits);
   if (rc) return rc;
@@ -437,6 +440,7 @@ int fk_dec_attn_splitkv_fwd(const void* q, const void* k_cache, const void* v_ca
 
   attn::Params p;
   p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_stride = q_stride;
   p.seqlens = cache_seqlens;
   p.o_part = o_partial;
   p.lse_part = lse_partial;
@@ -465,6 +469,26 @@ int fk_dec_attn_splitkv_fwd(const void* q, const void* k_cache, const void* v_ca
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p.G <= 4) return attn::launch_fwd<3>(tmK, tmV, p, st);
   return attn::launch_fwd<2>(tmK, tmV, p, st);
+}
+
+int fk_dec_attn_splitkv_fwd(const void* q, const void* k_cache, const void* v_cache,
+                            const int32_t* cache_seqlens, float* o_partial, float* lse_partial,
+                            int batch, int max_seqlen, int num_heads_q, int num_heads_kv,
+                            int head_dim, int num_splits, float softmax_scale, void* stream) {
+  return splitkv_fwd_impl(q, (long long)num_heads_q * head_dim, k_cache, v_cache, cache_seqlens, o_partial,
+                          lse_partial, batch, max_seqlen, num_heads_q, num_heads_kv, head_dim, num_splits,
+                          softmax_scale, stream);
+}
+
+int fk_dec_attn_fwd_ex(const void* q, long long q_batch_stride, const void* k_cache, const void* v_cache,
+                       const int32_t* cache_seqlens, void* out, float* lse, float* o_partial,
+                       float* lse_partial, int batch, int max_seqlen, int num_heads_q, int num_heads_kv,
+                       int head_dim, int num_splits, float softmax_scale, void* stream) {
+  int rc = splitkv_fwd_impl(q, q_batch_stride, k_cache, v_cache, cache_seqlens, o_partial, lse_partial, batch,
+                            max_seqlen, num_heads_q, num_heads_kv, head_dim, num_splits, softmax_scale, stream);
+  if (rc) return rc;
+  return fk_dec_attn_combine(o_partial, lse_partial, cache_seqlens, out, lse, batch, max_seqlen, num_heads_q,
+                             head_dim, num_splits, stream);
 }
 
 int fk_dec_attn_combine(const float* o_partial, const float* lse_partial,

@@ -1,0 +1,58 @@
+// KV-cache append for the decode step: write the new token's K and V rows of
+// every batch row into the padded cache at position cache_seqlens[b].
+//
+// Counterpart of the cache write in the reference's fused projection DAttn2
+// (python/cutedsl_kernels/decoding_attention/attempt2.py:276-286, which stores
+// the new rows at [P-M, P)), here for a ragged cache [B, Lmax, Hkv, D] indexed
+// by per-row lengths. The new rows are read straight out of the fused QKV
+// projection output (row stride and column offsets given), so no repacking
+// kernel runs between the QKV GEMM and attention.
+#include "common.cuh"
+#include "fk_b200.h"
+
+namespace fk {
+namespace kv {
+
+// One CTA per batch row; 16-byte vector copies.
+__global__ void __launch_bounds__(128) append_kernel(const __nv_bfloat16* __restrict__ src, long long src_stride,
+                                                     int k_col, int v_col, __nv_bfloat16* __restrict__ kc,
+                                                     __nv_bfloat16* __restrict__ vc, const int* seqlens_in,
+                                                     int* seqlens_out, int Lmax, int row_elems) {
+  const int b = blockIdx.x;
+  const int pos = seqlens_in[b];
+  __syncthreads();  // every thread has read the length before it may be overwritten in place
+  const bool ok = pos >= 0 && pos < Lmax;
+  if (ok) {
+    const uint4* ks = reinterpret_cast<const uint4*>(src + (size_t)b * src_stride + k_col);
+    const uint4* vs = reinterpret_cast<const uint4*>(src + (size_t)b * src_stride + v_col);
+    uint4* kd = reinterpret_cast<uint4*>(kc + ((size_t)b * Lmax + pos) * row_elems);
+    uint4* vd = reinterpret_cast<uint4*>(vc + ((size_t)b * Lmax + pos) * row_elems);
+    for (int i = threadIdx.x; i < row_elems / 8; i += blockDim.x) {
+      kd[i] = ks[i];
+      vd[i] = vs[i];
+    }
+  }
+  if (threadIdx.x == 0 && seqlens_out) seqlens_out[b] = ok ? pos + 1 : pos;
+}
+
+}  // namespace kv
+}  // namespace fk
+
+using namespace fk;
+
+extern "C" int fk_kv_append(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
+                            void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
+                            int max_seqlen, int num_heads_kv, int head_dim, void* stream) {
+  FK_CHECK_ARG(src && k_cache && v_cache && cache_seqlens, "null tensor pointer");
+  FK_CHECK_ARG(batch >= 1 && max_seqlen >= 1 && num_heads_kv >= 1 && head_dim >= 8, "sizes must be positive");
+  const int row = num_heads_kv * head_dim;
+  FK_CHECK_ARG(row % 8 == 0 && src_row_stride % 8 == 0 && k_col % 8 == 0 && v_col % 8 == 0,
+               "row length, stride and column offsets must be multiples of 8 elements");
+  FK_CHECK_ARG(((uintptr_t)src & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
+               "src and caches must be 16-byte aligned");
+  kv::append_kernel<<<batch, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), src_row_stride, k_col, v_col, static_cast<__nv_bfloat16*>(k_cache),
+      static_cast<__nv_bfloat16*>(v_cache), cache_seqlens, seqlens_out, max_seqlen, row);
+  FK_CHECK_CUDA(cudaGetLastError());
+  return kOk;
+}

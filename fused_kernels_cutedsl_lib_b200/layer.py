@@ -1,0 +1,250 @@
+"""Llama-style decoder-layer decode step built from this library's kernels.
+
+One step for a batch of B sequences, each generating one token:
+
+1. ``qkv = rms_norm(x, gamma_attn) @ W_qkv^T``      fused RMSNorm->QKV GEMM
+2. append the new K/V rows to the cache at ``cache_seqlens[b]``; lengths += 1
+3. ``attn = softmax(q K^T / sqrt(d)) V``             split-KV attention, q read in place from qkv
+4. ``h = x + attn @ W_o^T``                          GEMM with residual epilogue
+5. ``gu = silu(g) * u`` for ``[g; u] = rms_norm(h, gamma_ffn) @ W_gu^T``   fused RMSNorm->gate/up->SwiGLU
+6. ``y = h + gu @ W_down^T``                         GEMM with residual epilogue
+
+Seven launches, no host synchronisation and no torch compute on the path.
+The reference has no layer composition; this follows the decode path's full
+layer configuration (hidden 4096, 32 q / 8 kv heads of 128, FFN 14336).
+
+:class:`TPDecodeLayer` runs the same step on P GPUs (one process each):
+GEMMs are column-parallel (each rank holds 1/P of every weight's output
+features) with an NCCL all-gather of each GEMM's output, and attention is
+batch-parallel (each rank holds the KV cache of B/P rows), its output
+all-gathered over rows.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _native
+from ._tensors import ptr, stream_for
+from .decoding_attention import alloc_partials, default_num_splits
+from .gemm import alloc_workspace, linear, workspace_bytes
+from .sharding import column_range, shard_gate_up
+
+HEAD_DIM = 128
+
+
+@dataclass
+class LayerWeights:
+    gamma_attn: torch.Tensor  # [H]
+    w_qkv: torch.Tensor       # [(Hq + 2 Hkv) * 128, H]
+    w_o: torch.Tensor         # [H, Hq * 128]
+    gamma_ffn: torch.Tensor   # [H]
+    w_gate_up: torch.Tensor   # [2F, H], gate rows then up rows
+    w_down: torch.Tensor      # [H, F]
+
+    def as_dict(self) -> dict:
+        return dict(gamma_attn=self.gamma_attn, w_qkv=self.w_qkv, w_o=self.w_o, gamma_ffn=self.gamma_ffn,
+                    w_gate_up=self.w_gate_up, w_down=self.w_down)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.as_dict().values())
+
+
+def random_layer_weights(hidden=4096, ffn=14336, num_heads_q=32, num_heads_kv=8, seed=4, device="cuda",
+                         std=0.02) -> LayerWeights:
+    """bf16 weights N(0, std) and gains 1 + N(0, 0.1), drawn from ``seed``."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+    def gain(n):
+        return (1 + 0.1 * torch.randn(n, generator=g, device=device)).to(torch.bfloat16)
+
+    qkv = (num_heads_q + 2 * num_heads_kv) * HEAD_DIM
+    return LayerWeights(gamma_attn=gain(hidden), w_qkv=w(qkv, hidden), w_o=w(hidden, num_heads_q * HEAD_DIM),
+                        gamma_ffn=gain(hidden), w_gate_up=w(2 * ffn, hidden), w_down=w(hidden, ffn))
+
+
+def kv_append(qkv, k_cache, v_cache, cache_seqlens, num_heads_q, num_heads_kv, seqlens_out=None, stream=None):
+    """Write the new K/V rows held in ``qkv`` into the caches; lengths updated in ``seqlens_out``."""
+    B, L = k_cache.shape[0], k_cache.shape[1]
+    st = stream_for(qkv.device, stream)
+    out = cache_seqlens if seqlens_out is None else seqlens_out
+    _native.check(_native.load().fk_kv_append(
+        ptr(qkv), qkv.stride(0), num_heads_q * HEAD_DIM, (num_heads_q + num_heads_kv) * HEAD_DIM,
+        ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), B, L, num_heads_kv, HEAD_DIM, st))
+
+
+def attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_partial, lse_partial, num_splits,
+                       num_heads_q, num_heads_kv, softmax_scale=None, stream=None):
+    """Split-KV attention reading q from the first ``Hq*128`` columns of each ``qkv`` row."""
+    B, L = k_cache.shape[0], k_cache.shape[1]
+    scale = 1.0 / math.sqrt(HEAD_DIM) if softmax_scale is None else float(softmax_scale)
+    st = stream_for(qkv.device, stream)
+    _native.check(_native.load().fk_dec_attn_fwd_ex(
+        ptr(qkv), qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), ptr(lse),
+        ptr(o_partial), ptr(lse_partial), B, L, num_heads_q, num_heads_kv, HEAD_DIM, num_splits, scale, st))
+
+
+class DecodeLayer:
+    """Single-GPU decode step. ``layer(x, k_cache, v_cache, cache_seqlens) -> y``.
+
+    Appends the new token's K/V in place and advances ``cache_seqlens`` by one
+    (rows whose cache is full keep their length). Intermediate buffers are
+    allocated once per batch size and reused, so steady-state calls allocate
+    nothing and the step can be replayed inside a CUDA graph.
+    """
+
+    def __init__(self, weights: LayerWeights, num_heads_q=32, num_heads_kv=8, eps=1e-6, num_splits=None):
+        self.w = weights
+        self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
+        self.num_splits = num_splits
+        self.hidden = weights.w_qkv.shape[1]
+        self.ffn = weights.w_gate_up.shape[0] // 2
+        self.qkv_dim = weights.w_qkv.shape[0]
+        self._bufs: dict = {}
+
+    def buffers(self, B: int, L: int, device) -> dict:
+        key = (B, L, str(device))
+        b = self._bufs.get(key)
+        if b is None:
+            S = self.num_splits or default_num_splits(B, self.hkv, L)
+            o_p, l_p = alloc_partials(B, self.hq, S, device)
+            ws = max(workspace_bytes(B, n, k, sw) for n, k, sw in [
+                (self.qkv_dim, self.hidden, False), (self.hidden, self.hq * HEAD_DIM, False),
+                (self.ffn, self.hidden, True), (self.hidden, self.ffn, False)])
+            bf = dict(dtype=torch.bfloat16, device=device)
+            b = dict(S=S, o_p=o_p, l_p=l_p, ws=alloc_workspace(ws, device),
+                     qkv=torch.empty(B, self.qkv_dim, **bf), attn=torch.empty(B, self.hq * HEAD_DIM, **bf),
+                     lse=torch.empty(B, self.hq, dtype=torch.float32, device=device),
+                     h=torch.empty(B, self.hidden, **bf), gu=torch.empty(B, self.ffn, **bf),
+                     y=torch.empty(B, self.hidden, **bf))
+            self._bufs[key] = b
+        return b
+
+    def __call__(self, x, k_cache, v_cache, cache_seqlens, out=None, stream=None):
+        B, L = x.shape[0], k_cache.shape[1]
+        b = self.buffers(B, L, x.device)
+        w, ws = self.w, b["ws"]
+        linear(x, w.w_qkv, b["qkv"], gamma=w.gamma_attn, eps=self.eps, workspace=ws, stream=stream)
+        kv_append(b["qkv"], k_cache, v_cache, cache_seqlens, self.hq, self.hkv, stream=stream)
+        attention_from_qkv(b["qkv"], k_cache, v_cache, cache_seqlens, b["attn"], b["lse"], b["o_p"], b["l_p"],
+                           b["S"], self.hq, self.hkv, stream=stream)
+        linear(b["attn"], w.w_o, b["h"], residual=x, workspace=ws, stream=stream)
+        linear(b["h"], w.w_gate_up, b["gu"], gamma=w.gamma_ffn, eps=self.eps, w_up=w.w_gate_up,
+               up_row_offset=self.ffn, workspace=ws, stream=stream)
+        y = b["y"] if out is None else out
+        linear(b["gu"], w.w_down, y, residual=b["h"], workspace=ws, stream=stream)
+        return y
+
+
+def shard_layer_weights(full: LayerWeights, rank: int, world: int, num_heads_q=32, num_heads_kv=8) -> LayerWeights:
+    """Column (output-feature) shard of every weight for tensor-parallel rank ``rank``."""
+    qkv_lo, qkv_hi = column_range(full.w_qkv.shape[0], rank, world)
+    h_lo, h_hi = column_range(full.w_o.shape[0], rank, world)
+    return LayerWeights(
+        gamma_attn=full.gamma_attn, gamma_ffn=full.gamma_ffn,
+        w_qkv=full.w_qkv[qkv_lo:qkv_hi].contiguous(),
+        w_o=full.w_o[h_lo:h_hi].contiguous(),
+        w_gate_up=shard_gate_up(full.w_gate_up, rank, world),
+        w_down=full.w_down[h_lo:h_hi].contiguous())
+
+
+class KernelOps:
+    """The compute steps of the TP layer, on this library's kernels (the product path)."""
+
+    def __init__(self, num_heads_q, num_heads_kv, eps):
+        self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
+        self._ws: dict = {}
+
+    def _wsp(self, x):
+        key = str(x.device)
+        if key not in self._ws:
+            self._ws[key] = alloc_workspace(64 << 20, x.device)
+        return self._ws[key]
+
+    def rms_linear(self, x, gamma, w, out):
+        return linear(x, w, out, gamma=gamma, eps=self.eps, workspace=self._wsp(x))
+
+    def linear(self, x, w, out, residual=None):
+        return linear(x, w, out, residual=residual, workspace=self._wsp(x))
+
+    def rms_swiglu(self, x, gamma, w_gate_up, out):
+        n = w_gate_up.shape[0] // 2
+        return linear(x, w_gate_up, out, gamma=gamma, eps=self.eps, w_up=w_gate_up, up_row_offset=n,
+                      workspace=self._wsp(x))
+
+    def append_and_attend(self, qkv, k_cache, v_cache, cache_seqlens, out):
+        B, L = k_cache.shape[0], k_cache.shape[1]
+        S = default_num_splits(B, self.hkv, L)
+        o_p, l_p = alloc_partials(B, self.hq, S, qkv.device)
+        lse = torch.empty(B, self.hq, dtype=torch.float32, device=qkv.device)
+        kv_append(qkv, k_cache, v_cache, cache_seqlens, self.hq, self.hkv)
+        attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, self.hq, self.hkv)
+        return out
+
+
+class TPDecodeLayer:
+    """Decode step on P ranks: column-parallel GEMMs + batch-parallel attention.
+
+    ``weights`` is this rank's :func:`shard_layer_weights` shard; ``rows`` the
+    contiguous block of batch rows whose KV cache this rank holds (equal blocks
+    on every rank). Activations entering a GEMM are replicated; each GEMM's
+    output shard is all-gathered (``all_gather_into_tensor``) and re-laid out
+    from [P, B, n/P] to [B, n]. Attention output rows are gathered the same way
+    (already row-contiguous). ``ops`` defaults to the CUDA kernels.
+    """
+
+    def __init__(self, weights: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6, ops=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.w = weights
+        self.hq, self.hkv = num_heads_q, num_heads_kv
+        self.ops = ops if ops is not None else KernelOps(num_heads_q, num_heads_kv, eps)
+        for name, n in (("w_qkv", weights.w_qkv.shape[0] * self.world), ("w_o", weights.w_o.shape[0] * self.world),
+                        ("w_down", weights.w_down.shape[0] * self.world)):
+            if n % (128 * self.world):
+                raise ValueError(f"{name}: {n} output features do not split into equal 128-column blocks "
+                                 f"over {self.world} ranks")
+
+    def _gather_cols(self, part: torch.Tensor) -> torch.Tensor:
+        """[B, n/P] on every rank -> [B, n] (rank-major column blocks)."""
+        B, c = part.shape
+        buf = torch.empty(self.world * B, c, dtype=part.dtype, device=part.device)
+        self.dist.all_gather_into_tensor(buf, part.contiguous(), group=self.group)
+        return buf.view(self.world, B, c).permute(1, 0, 2).reshape(B, self.world * c)
+
+    def _gather_rows(self, part: torch.Tensor) -> torch.Tensor:
+        buf = torch.empty(self.world * part.shape[0], *part.shape[1:], dtype=part.dtype, device=part.device)
+        self.dist.all_gather_into_tensor(buf, part.contiguous(), group=self.group)
+        return buf
+
+    def __call__(self, x, k_cache, v_cache, cache_seqlens):
+        """x [B, H] replicated; k/v caches and lengths hold this rank's B/P rows. Returns y [B, H]."""
+        B = x.shape[0]
+        Bl = k_cache.shape[0]
+        if Bl * self.world != B:
+            raise ValueError(f"batch {B} must split evenly: {Bl} rows per rank x {self.world} ranks")
+        w, ops = self.w, self.ops
+        dt = dict(dtype=x.dtype, device=x.device)
+        qkv = self._gather_cols(ops.rms_linear(x, w.gamma_attn, w.w_qkv, torch.empty(B, w.w_qkv.shape[0], **dt)))
+        r0 = self.rank * Bl
+        my_qkv = qkv[r0:r0 + Bl].contiguous()
+        attn_local = ops.append_and_attend(my_qkv, k_cache, v_cache, cache_seqlens,
+                                           torch.empty(Bl, self.hq * HEAD_DIM, **dt))
+        attn = self._gather_rows(attn_local)
+        c_lo, c_hi = column_range(x.shape[1], self.rank, self.world)
+        # residual added in the GEMM epilogue on this rank's column block
+        h = self._gather_cols(ops.linear(attn, w.w_o, torch.empty(B, c_hi - c_lo, **dt),
+                                         residual=x[:, c_lo:c_hi].contiguous()))
+        gu = self._gather_cols(ops.rms_swiglu(h, w.gamma_ffn, w.w_gate_up,
+                                              torch.empty(B, w.w_gate_up.shape[0] // 2, **dt)))
+        return self._gather_cols(ops.linear(gu, w.w_down, torch.empty(B, c_hi - c_lo, **dt),
+                                            residual=h[:, c_lo:c_hi].contiguous()))

@@ -97,6 +97,26 @@ FK_API int fk_dec_attn_fwd(const void* q, const void* k_cache, const void* v_cac
                     int num_heads_kv, int head_dim, int num_splits, float softmax_scale,
                     void* stream);
 
+/* Both passes with q read at a row stride: row b of q starts q_batch_stride
+ * elements after row b-1 (its Hq x 128 values contiguous). Lets attention read
+ * q straight out of a fused QKV projection output [B, (Hq + 2 Hkv) * 128]. */
+FK_API int fk_dec_attn_fwd_ex(const void* q, long long q_batch_stride, const void* k_cache,
+                              const void* v_cache, const int32_t* cache_seqlens, void* out, float* lse,
+                              float* o_partial, float* lse_partial, int batch, int max_seqlen,
+                              int num_heads_q, int num_heads_kv, int head_dim, int num_splits,
+                              float softmax_scale, void* stream);
+
+/* KV-cache append: for each row b with 0 <= cache_seqlens[b] < max_seqlen,
+ * copy the new K row (src + b*src_row_stride + k_col, num_heads_kv*head_dim
+ * bf16) and V row (… + v_col) into k_cache/v_cache[b, cache_seqlens[b]] and
+ * write seqlens_out[b] = cache_seqlens[b] + 1 (rows already full are left
+ * alone and keep their length). seqlens_out may alias cache_seqlens or be
+ * null. Counterpart of the cache write of the reference's DAttn2
+ * (python/cutedsl_kernels/decoding_attention/attempt2.py:276-286). */
+FK_API int fk_kv_append(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
+                        void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
+                        int max_seqlen, int num_heads_kv, int head_dim, void* stream);
+
 /* ---- linear family: y[M, N] = epilogue(x[M, K] . W[N, K]^T) ---------------
  * x bf16 [M, K] (K % 8 == 0, 16-byte aligned), W bf16 [N, K] (row = output
  * feature), y bf16 [M, N], fp32 accumulation. M <= 16 runs the persistent

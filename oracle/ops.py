@@ -117,8 +117,9 @@ def decode_layer(x, weights: dict, k_cache, v_cache, cache_seqlens, eps=1e-6,
 
     Composition of the functions above (the full-layer config of the decode
     path): ``h = x + Wo·attn(rmsnorm(x)·Wqkv)``, ``y = h + Wdown·swiglu(rmsnorm(h)·Wgu)``.
-    The new token's K/V are appended at position ``cache_seqlens[b]`` of copies of
-    the caches and attention runs over ``cache_seqlens[b] + 1`` keys.
+    The new token's K/V are appended after the first ``cache_seqlens[b]`` keys of
+    each row (the caches themselves are not modified) and attention runs over
+    ``cache_seqlens[b] + 1`` keys.
     With ``round_intermediates`` every hand-off between kernels is rounded to
     bf16, as the kernels' bf16 outputs are.
 
@@ -135,14 +136,15 @@ def decode_layer(x, weights: dict, k_cache, v_cache, cache_seqlens, eps=1e-6,
     k_new = qkv[:, num_heads_q * D:(num_heads_q + num_heads_kv) * D].reshape(B, num_heads_kv, D)
     v_new = qkv[:, (num_heads_q + num_heads_kv) * D:].reshape(B, num_heads_kv, D)
     lens = cache_seqlens.detach().to("cpu", torch.int64)
-    kc = _cpu32(k_cache).clone()
-    vc = _cpu32(v_cache).clone()
-    for b in range(B):
-        kc[b, lens[b]] = k_new[b]
-        vc[b, lens[b]] = v_new[b]
+    attn = torch.empty(B, num_heads_q * D)
+    for b in range(B):  # per row: the cached keys plus the appended one; no full-cache copy
+        L = int(lens[b])
+        kb = torch.cat([_cpu32(k_cache[b, :L]), k_new[b:b + 1]], 0).unsqueeze(0)
+        vb = torch.cat([_cpu32(v_cache[b, :L]), v_new[b:b + 1]], 0).unsqueeze(0)
+        o, _ = decode_attention(q[b:b + 1], kb, vb, torch.tensor([L + 1]))
+        attn[b] = o.reshape(-1)
     new_lens = (lens + 1).to(torch.int32)
-    attn, _ = decode_attention(q, kc, vc, new_lens)
-    attn = rnd(attn.reshape(B, num_heads_q * D))
+    attn = rnd(attn)
     h = rnd(xf + linear(attn, weights["w_o"]))
     gu = rnd(swiglu(rmsnorm(h, weights["gamma_ffn"], eps), weights["w_gate_up"]))
     y = h + linear(gu, weights["w_down"])
