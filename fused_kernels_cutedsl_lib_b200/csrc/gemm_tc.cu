@@ -15,8 +15,9 @@
 //               x box {64 k, N_mma rows}, gamma box {64} per stage
 //   warp 1      allocates TMEM, one lane issues tcgen05.mma (4 x K=16 per
 //               stage) and tcgen05.commit to free stages / publish results
-//   warps 2-5   RMSNorm: multiply the x tile by gamma in shared memory (bf16,
-//               one rounding) and accumulate the per-token sum of squares;
+//   warps 2-5   RMSNorm: multiply the x tile by gamma in shared memory in fp32,
+//               split it into bf16 hi (in place) + lo (second tile) parts that
+//               both go through the MMA, and accumulate the per-token sum of squares;
 //               epilogue: tcgen05.ld the accumulators 16 columns at a time,
 //               scale by rsqrt(ss/K + eps), SwiGLU, residual, bf16 store
 // Work is split stream-K over (row block, k block) exactly as in the skinny
@@ -44,8 +45,10 @@ struct Layout {
   static constexpr int X_OFF = W_BYTES;
   static constexpr int X_BYTES = NMMA * 128;
   static constexpr int G_OFF = X_OFF + X_BYTES;
+  // RMSNorm: the low bf16 part of x*gamma, same swizzled layout as the x tile.
+  static constexpr int XL_OFF = (G_OFF + 128 + 1023) / 1024 * 1024;
   static constexpr int TX = W_BYTES + X_BYTES + (NORM ? 128 : 0);
-  static constexpr int STAGE_BYTES = (G_OFF + (NORM ? 128 : 0) + 1023) / 1024 * 1024;
+  static constexpr int STAGE_BYTES = NORM ? XL_OFF + X_BYTES : (G_OFF + 1023) / 1024 * 1024;
   static constexpr int STAGES_FIT = (int)((kSmemBudget - 1024 - 2048) / STAGE_BYTES);
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int ACC_COLS = NMMA * (SWIGLU ? 2 : 1);
@@ -226,6 +229,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const uint64_t du = umma_desc_sw128(sb + WBOX);
               umma_bf16(tmem + NMMA, du + 2 * kk, db + 2 * kk, idesc, acc);
             }
+            if (NORM) {  // low part of x*gamma into the same accumulators
+              const uint64_t dl = umma_desc_sw128(sb + LY::XL_OFF);
+              umma_bf16(tmem, da + 2 * kk, dl + 2 * kk, idesc, 1u);
+              if (SWIGLU) umma_bf16(tmem + NMMA, umma_desc_sw128(sb + WBOX) + 2 * kk, dl + 2 * kk, idesc, 1u);
+            }
           }
           umma_commit(&empty[stage]);
         }
@@ -270,24 +278,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             const int tok = et + half * 128;
-            if (tok < NMMA && tok < p.M) {
+            if (tok < NMMA) {  // rows >= M are TMA zero-fill: their lo part is written as zero too
               uint4* xr = reinterpret_cast<uint4*>(st + LY::X_OFF + tok * 128);
+              uint4* xl = reinterpret_cast<uint4*>(st + LY::XL_OFF + tok * 128);
               float ssl = 0.f;
 #pragma unroll
               for (int pc = 0; pc < 8; ++pc) {
                 uint4 xv = xr[pc];
+                uint4 lv;
                 const uint4 gv = gam[pc ^ (tok & 7)];
                 uint32_t* xw = reinterpret_cast<uint32_t*>(&xv);
+                uint32_t* lw = reinterpret_cast<uint32_t*>(&lv);
                 const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[e]));
+                  const float2 gg = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
                   ssl = fmaf(f.x, f.x, fmaf(f.y, f.y, ssl));
-                  __nv_bfloat162 prod = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&xw[e]),
-                                                *reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
-                  xw[e] = *reinterpret_cast<uint32_t*>(&prod);
+                  const float p0 = f.x * gg.x, p1 = f.y * gg.y;
+                  const __nv_bfloat162 hi = __floats2bfloat162_rn(p0, p1);
+                  const float2 hf = __bfloat1622float2(hi);
+                  xw[e] = *reinterpret_cast<const uint32_t*>(&hi);
+                  lw[e] = pack_bf16x2(p0 - hf.x, p1 - hf.y);
                 }
                 xr[pc] = xv;
+                xl[pc] = lv;
               }
               if (half == 0) ss0 += ssl; else ss1 += ssl;
             }

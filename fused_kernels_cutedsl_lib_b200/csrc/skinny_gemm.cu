@@ -28,7 +28,8 @@
 //
 // Epilogues:
 //   plain    y = acc (+ residual)
-//   RMSNorm  x is multiplied by gamma on the B fragments (bf16, one rounding);
+//   RMSNorm  x is multiplied by gamma on the B fragments in fp32 and split
+//            into bf16 hi + lo parts, both fed to the MMA (~16-bit mantissa);
 //            the per-token sum of squares of x is accumulated from the same
 //            fragments and y = acc * rsqrt(ss/K + eps) — the normalisation of
 //            rmsnorm_linear/attempt1/gemm.py:509-547 computed in the mainloop,
@@ -202,28 +203,35 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ldsm_x4(swz128(base, t * 8 + r, 2 * (s & 3) + j), bx[t][s][0], bx[t][s][1], bx[t][s + 1][0],
                   bx[t][s + 1][1]);
         }
+      // RMSNorm: x*gamma is split into bf16 hi + lo parts (hi = bf16(x*gamma),
+      // lo = bf16(x*gamma - hi)) and both are multiplied into the same
+      // accumulators, so the product keeps ~16 mantissa bits instead of 8.
+      uint32_t bl[NORM ? NT : 1][8][2];
       if (NORM) {
         const uint32_t* gam = reinterpret_cast<const uint32_t*>(st + LY::G_OFF);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const uint32_t g0 = gam[(16 * s + 2 * c) >> 1];
-          const uint32_t g1 = gam[(16 * s + 8 + 2 * c) >> 1];
+          const float2 g0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gam[(16 * s + 2 * c) >> 1]));
+          const float2 g1 =
+              __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gam[(16 * s + 8 + 2 * c) >> 1]));
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
+            const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bx[t][s][0]));
+            const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bx[t][s][1]));
             if (warp == 0) {
-              const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bx[t][s][0]));
-              const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bx[t][s][1]));
               ss[t] = fmaf(f0.x, f0.x, ss[t]);
               ss[t] = fmaf(f0.y, f0.y, ss[t]);
               ss[t] = fmaf(f1.x, f1.x, ss[t]);
               ss[t] = fmaf(f1.y, f1.y, ss[t]);
             }
-            __nv_bfloat162 v0 = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bx[t][s][0]),
-                                        *reinterpret_cast<const __nv_bfloat162*>(&g0));
-            __nv_bfloat162 v1 = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bx[t][s][1]),
-                                        *reinterpret_cast<const __nv_bfloat162*>(&g1));
-            bx[t][s][0] = *reinterpret_cast<uint32_t*>(&v0);
-            bx[t][s][1] = *reinterpret_cast<uint32_t*>(&v1);
+            const float p0 = f0.x * g0.x, p1 = f0.y * g0.y, p2 = f1.x * g1.x, p3 = f1.y * g1.y;
+            const __nv_bfloat162 h0 = __floats2bfloat162_rn(p0, p1);
+            const __nv_bfloat162 h1 = __floats2bfloat162_rn(p2, p3);
+            const float2 q0 = __bfloat1622float2(h0), q1 = __bfloat1622float2(h1);
+            bx[t][s][0] = *reinterpret_cast<const uint32_t*>(&h0);
+            bx[t][s][1] = *reinterpret_cast<const uint32_t*>(&h1);
+            bl[NORM ? t : 0][s][0] = pack_bf16x2(p0 - q0.x, p1 - q0.y);
+            bl[NORM ? t : 0][s][1] = pack_bf16x2(p2 - q1.x, p3 - q1.y);
           }
         }
       }
@@ -236,7 +244,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ldsm_x4(swz128(abase + (s >> 2) * WBOX_BYTES, 16 * warp + (j & 1) * 8 + r, 2 * (s & 3) + (j >> 1)),
                   af[0], af[1], af[2], af[3]);
 #pragma unroll
-          for (int t = 0; t < NT; ++t) mma_bf16_16816(acc[a][s & 1][t], af, bx[t][s][0], bx[t][s][1]);
+          for (int t = 0; t < NT; ++t) {
+            mma_bf16_16816(acc[a][s & 1][t], af, bx[t][s][0], bx[t][s][1]);
+            if (NORM) mma_bf16_16816(acc[a][(s & 1) ^ 1][t], af, bl[NORM ? t : 0][s][0], bl[NORM ? t : 0][s][1]);
+          }
         }
       }
       __syncwarp();
