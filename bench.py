@@ -353,6 +353,96 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_layer(args):
+    """Config 5: full decoder-layer decode step, B=128 at context 8192 (tensor-parallel for N > 1)."""
+    import torch.distributed as dist
+
+    from fused_kernels_cutedsl_lib_b200 import _native
+    from fused_kernels_cutedsl_lib_b200.layer import (DecodeLayer, TPDecodeLayer, random_layer_weights,
+                                                      shard_layer_weights)
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    B, ctx, H, F, HQ, HKV = 128, 8192, 4096, 14336, 32, 8
+    Lmax = ctx + args.warmup + 2 * args.steps + 16
+    full = random_layer_weights(H, F, HQ, HKV, seed=4, device=dev)
+    Bl = B // world
+    g = torch.Generator(device=dev).manual_seed(4 * 1000 + rank)
+    k = torch.empty(Bl, Lmax, HKV, 128, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    v = torch.empty_like(k).normal_(generator=g)
+    lens = torch.full((Bl,), ctx, dtype=torch.int32, device=dev)
+    gx = torch.Generator(device=dev).manual_seed(44)
+    x = torch.randn(B, H, generator=gx, device=dev).to(torch.bfloat16)
+    if world > 1:
+        layer = TPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
+    else:
+        layer = DecodeLayer(full, HQ, HKV)
+    wbytes = full.nbytes()
+    del full
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        layer(x, k, v, lens)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.mark_start()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        layer(x, k, v, lens)
+    b.record(stream)
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    clk = clocks.stop()
+    ms = a.elapsed_time(b) / args.steps
+    if _native.device_error() != 0:
+        raise RuntimeError("device error word set during the bench")
+    # e2e: x H2D from pinned host, y D2H, inside the timed region
+    x_h = x.cpu().pin_memory()
+    y_h = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x)
+    a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a2.record(stream)
+    for _ in range(args.steps):
+        x_d.copy_(x_h, non_blocking=True)
+        y = layer(x_d, k, v, lens)
+        y_h.copy_(y, non_blocking=True)
+    b2.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a2.elapsed_time(b2) / args.steps
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    if rank == 0:
+        kv_bytes = B * (ctx + args.warmup + args.steps) * HKV * 128 * 4  # approx. mid-run lengths
+        peak, kind = _peaks()
+        print(json.dumps({
+            "metric": "decode-layer tokens/s (Llama-3-8B-shaped layer, B=128, ctx 8192)",
+            "value": round(B / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights seed 4, N(0,1) KV)",
+            "config": {"workload": "decode_layer_config5", "batch": B, "context": ctx, "hidden": H, "ffn": F,
+                       "heads_q": HQ, "heads_kv": HKV,
+                       "parallelism": "single GPU" if world == 1 else f"tp{world} GEMMs + batch-sharded attention",
+                       "l2": "weights 436 MB + KV 4.3 GB per step exceed L2"},
+            "bytes_per_step": wbytes + kv_bytes,
+            "achieved_TBps": round((wbytes + kv_bytes) / world / (ms * 1e-3) / 1e12, 3),
+            "peak_GBps": peak, "peak_kind": kind,
+            "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+            "gpu_launches": args.steps * (7 if world == 1 else 7),
+            "clocks": clk,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -361,11 +451,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["attention", "layer"], default="attention",
+                    help="attention: config 2 split-KV decode attention (headline); layer: config 5 decode step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "layer":
+        run_layer(args)
     else:
         run_ours(args)
 
