@@ -1,4 +1,4 @@
-// tcgen05/TMEM GEMM for 16 < M <= 256 tokens per tile on sm_100a:
+// tcgen05/TMEM GEMM for M > 16 tokens on sm_100a:
 //   y[M, N] = epilogue( x[M, K] . W[N, K]^T )
 //
 // Replaces the reference's wgmma GEMMs (Gemm4SM90,
@@ -7,22 +7,29 @@
 // for M large enough to be a dense contraction. Operands are swapped as in the
 // reference's skinny projection (decoding_attention/attempt2.py:120-121): a
 // 128-row W tile is the UMMA M side and the tokens are the N side
-// (N_mma = M rounded up to 16, <= 256), so the accumulator is 128 TMEM lanes
-// (output features) x N_mma columns (tokens). No cluster multicast.
+// (N_mma = tokens rounded up to 32/64/128/256), so the accumulator is 128 TMEM
+// lanes (output features) x N_mma columns (tokens). No cluster multicast.
 //
 // Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: W box {64 k, 128 rows} (+ the SwiGLU up rows),
-//               x box {64 k, N_mma rows}, gamma box {64} per stage
+//   warp 0      TMA producer: W box {64 k, 128 rows} (+ the SwiGLU up rows)
+//               and x box {64 k, N_mma rows} per stage
 //   warp 1      allocates TMEM, one lane issues tcgen05.mma (4 x K=16 per
-//               stage) and tcgen05.commit to free stages / publish results
-//   warps 2-5   RMSNorm: multiply the x tile by gamma in shared memory in fp32,
-//               split it into bf16 hi (in place) + lo (second tile) parts that
-//               both go through the MMA, and accumulate the per-token sum of squares;
-//               epilogue: tcgen05.ld the accumulators 16 columns at a time,
-//               scale by rsqrt(ss/K + eps), SwiGLU, residual, bf16 store
-// Work is split stream-K over (row block, k block) exactly as in the skinny
-// kernel: partial row blocks go to the caller's workspace and the last
-// contributor (counter) merges them in contributor order and resets the counter.
+//               stage) and tcgen05.commit to free stages / publish results;
+//               frees TMEM once the epilogue warps report done
+//   warps 2-5   epilogue: tcgen05.ld the accumulators 16 columns at a time,
+//               RMSNorm scale, SwiGLU, residual, bf16 store
+// Work is split stream-K over (row block, k block): every CTA streams the same
+// number of weight bytes. Row blocks finished inside one CTA are written by the
+// GEMM; split ones leave fp32 partials in the caller's workspace and a
+// reduction kernel, launched as a programmatic dependent of the GEMM, sums them
+// in contributor order (deterministic) with one CTA per (row block, 8 tokens).
+//
+// RMSNorm: a prologue kernel (rms_split_kernel) computes rstd per token and
+// splits x*gamma into bf16 hi and lo parts, stored as token rows [0, Mp) and
+// [Mp, 2Mp) of a workspace matrix; the GEMM multiplies both in one MMA (N =
+// 2Mp) and the epilogue adds the two halves and scales by rstd. x*gamma is
+// thus represented to ~16 mantissa bits and computed once per call instead of
+// once per k block per CTA.
 #include <math.h>
 
 #include "common.cuh"
@@ -31,48 +38,55 @@
 namespace fk {
 namespace tc {
 
-constexpr int BM = 128;       // W rows per row block (UMMA M)
-constexpr int BK = 64;        // k per stage: one 128B swizzle atom of bf16
-constexpr int NTHREADS = 192; // 6 warps
+constexpr int BM = 128;         // W rows per row block (UMMA M)
+constexpr int BK = 64;          // k per stage: one 128B swizzle atom of bf16
+constexpr int NTHREADS = 192;   // 6 warps
 constexpr int EPI_WARP0 = 2;
 constexpr int EPI_THREADS = 128;
 constexpr int WBOX = BM * 128;  // 16 KB
+constexpr int NORM_TILE = 128;  // tokens per launch with RMSNorm (hi + lo = 256 columns)
 constexpr size_t kSmemBudget = 227 * 1024;
+constexpr int kMaxGrid = 192;   // persistent grid bound (148 SMs on B200)
 
-template <int NMMA, bool SWIGLU, bool NORM>
+template <int NMMA, bool SWIGLU>
 struct Layout {
   static constexpr int W_BYTES = WBOX * (SWIGLU ? 2 : 1);
   static constexpr int X_OFF = W_BYTES;
   static constexpr int X_BYTES = NMMA * 128;
-  static constexpr int G_OFF = X_OFF + X_BYTES;
-  // RMSNorm: the low bf16 part of x*gamma, same swizzled layout as the x tile.
-  static constexpr int XL_OFF = (G_OFF + 128 + 1023) / 1024 * 1024;
-  static constexpr int TX = W_BYTES + X_BYTES + (NORM ? 128 : 0);
-  static constexpr int STAGE_BYTES = NORM ? XL_OFF + X_BYTES : (G_OFF + 1023) / 1024 * 1024;
-  static constexpr int STAGES_FIT = (int)((kSmemBudget - 1024 - 2048) / STAGE_BYTES);
+  static constexpr int TX = W_BYTES + X_BYTES;
+  static constexpr int STAGE_BYTES = (X_OFF + X_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGES_FIT = (int)((kSmemBudget - 4096) / (STAGE_BYTES + 16));
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int ACC_COLS = NMMA * (SWIGLU ? 2 : 1);
   static constexpr int TMEM_COLS = ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
                                    : ACC_COLS <= 256 ? 256 : 512;
-  // barriers: full, xready, empty per stage + acc_full + acc_empty; tmem addr; flag; ss[256]
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (3 * STAGES + 2) * 8 + 16 + 256 * 4;
+  // barriers: full + empty per stage, acc_full, acc_empty, done; TMEM address
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (2 * STAGES + 3) * 8 + 16;
 };
 
-__host__ __device__ constexpr int slot_floats(int nmma, bool swiglu) { return nmma * BM * (swiglu ? 2 : 1) + nmma; }
+__host__ __device__ constexpr int slot_floats(int nmma, bool swiglu) { return nmma * BM * (swiglu ? 2 : 1); }
 
 struct Params {
   const __nv_bfloat16* residual;
   __nv_bfloat16* y;
-  int* counters;
+  const float* rstd;  // [Mp] (RMSNorm) or null
   float* partials;
   int* err;
   int M, N, K, KI, num_rb, up_row_offset;
+  int Mp;             // RMSNorm: column offset of the lo half (tokens rounded up to 16)
   long long total;
   int G;
-  float eps, inv_k;
+  int starts[kMaxGrid + 1];  // starts[c] = c * total / G: first iteration of CTA c
 };
 
-__device__ __forceinline__ long long it_start(const Params& p, int c) { return (long long)c * p.total / p.G; }
+#ifdef FK_TC_TRACE
+__device__ unsigned long long g_tc_trace[256 * 32];
+#define TC_TRACE(i) g_tc_trace[blockIdx.x * 32 + (i)] = global_timer_ns()
+#else
+#define TC_TRACE(i) ((void)0)
+#endif
+
+__device__ __forceinline__ long long it_start(const Params& p, int c) { return p.starts[c]; }
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
 
 // UMMA shared-memory descriptor: K-major operand, 128B swizzle, 8-row groups 1024 B apart.
@@ -86,7 +100,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int n) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -112,41 +125,59 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 accumulator columns for tokens [c0, c0+16) of one matrix; with RMSNorm the
+// hi and lo halves are added (the rstd scale is applied by the caller).
+template <bool NORM>
+__device__ __forceinline__ void load_tokens(uint32_t trow, int c0, int Mp, float (&a)[16]) {
+  tmem_ld16(trow + c0, a);
+  if (NORM) {
+    float b[16];
+    tmem_ld16(trow + Mp + c0, b);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] += b[i];
+  }
+}
+
+__device__ __forceinline__ void store_out(const Params& p, int m, int col, float g, float u, bool swiglu) {
+  float rs = p.rstd ? __ldg(p.rstd + m) : 1.f;
+  float val = swiglu ? silu_f(g * rs) * (u * rs) : g * rs;
+  const size_t off = (size_t)m * p.N + col;
+  if (p.residual) val += __bfloat162float(p.residual[off]);
+  p.y[off] = __float2bfloat16_rn(val);
+}
+
 template <int NMMA, bool SWIGLU, bool NORM>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWu,
-                   const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG, Params p) {
-  using LY = Layout<NMMA, SWIGLU, NORM>;
+                   const __grid_constant__ CUtensorMap tmX, Params p) {
+  using LY = Layout<NMMA, SWIGLU>;
   constexpr int S = LY::STAGES;
-  constexpr int NMAT = SWIGLU ? 2 : 1;
   constexpr int SLOT = slot_floats(NMMA, SWIGLU);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * LY::STAGE_BYTES);
-  uint64_t* xready = full + S;
-  uint64_t* empty = xready + S;
+  uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_sm = reinterpret_cast<uint32_t*>(acc_empty + 1);
-  int* flag_sm = reinterpret_cast<int*>(tmem_sm + 1);
-  volatile int* abort_sm = flag_sm + 1;
-  float* ss_sm = reinterpret_cast<float*>(tmem_sm + 4);  // [256]
+  uint64_t* done = acc_empty + 1;
+  uint32_t* tmem_sm = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
   const long long it_begin = it_start(p, cta);
   const long long it_end = it_start(p, cta + 1);
+  // token columns the epilogue reads: the valid tokens (NORM: of each half)
+  const int mcols = NORM ? p.M : (p.M < NMMA ? p.M : NMMA);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&xready[i], 4);
       mbar_init(&empty[i], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 4);
-    *abort_sm = 0;
+    mbar_init(done, 4);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -158,6 +189,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_sm;
+  if (threadIdx.x == 0) TC_TRACE(0);
+  // The split-row-block reduction kernel may be scheduled as soon as SMs free
+  // up; it waits (griddepcontrol.wait) for this grid to complete before reading.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -166,34 +201,47 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tma_prefetch_desc(&tmX);
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      for (long long it = it_begin; it < it_end; ++it) {
+      // Weights never depend on the previous kernel on the stream: the first
+      // ring of W tiles is requested before waiting for it (programmatic
+      // dependent launch); x is loaded only after griddepcontrol.wait.
+      const long long pre_end = it_begin + S < it_end ? it_begin + S : it_end;
+      for (long long it = it_begin; it < pre_end; ++it) {
         const int rb = (int)(it / p.KI);
         const int k0 = (int)(it - (long long)rb * p.KI) * BK;
-        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) {
-          *abort_sm = 1;
-          break;
-        }
+        const int s = (int)(it - it_begin);
+        uint8_t* st = smem + s * LY::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], LY::TX);
+        tma_load_2d(st, &tmW, &full[s], k0, rb * BM, pol_w);
+        if (SWIGLU) tma_load_2d(st + WBOX, &tmWu, &full[s], k0, p.up_row_offset + rb * BM, pol_w);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (long long it = it_begin; it < pre_end; ++it) {
+        const int k0 = (int)(it - (it / p.KI) * p.KI) * BK;
+        const int s = (int)(it - it_begin);
+        tma_load_2d(smem + s * LY::STAGE_BYTES + LY::X_OFF, &tmX, &full[s], k0, 0, pol_x);
+      }
+      int stage = (int)((pre_end - it_begin) % S);
+      uint32_t phase = (pre_end - it_begin) >= S ? 1u : 0u;
+      for (long long it = pre_end; it < it_end; ++it) {
+        const int rb = (int)(it / p.KI);
+        const int k0 = (int)(it - (long long)rb * p.KI) * BK;
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) break;
         uint8_t* st = smem + stage * LY::STAGE_BYTES;
         mbar_arrive_expect_tx(&full[stage], LY::TX);
         tma_load_2d(st, &tmW, &full[stage], k0, rb * BM, pol_w);
         if (SWIGLU) tma_load_2d(st + WBOX, &tmWu, &full[stage], k0, p.up_row_offset + rb * BM, pol_w);
         tma_load_2d(st + LY::X_OFF, &tmX, &full[stage], k0, 0, pol_x);
-        if (NORM) {
-          asm volatile(
-              "cp.async.bulk.tensor.1d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-              " [%0], [%1, {%2}], [%3], %4;" ::"r"(smem_u32(st + LY::G_OFF)),
-              "l"(reinterpret_cast<uint64_t>(&tmG)), "r"(k0), "r"(smem_u32(&full[stage])), "l"(pol_x)
-              : "memory");
-        }
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
         }
       }
     }
-  } else if (warp == 1) {
+    __syncwarp();
+    return;
+  }
+
+  if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
     constexpr uint32_t idesc = umma_idesc_bf16(NMMA);
     int stage = 0;
@@ -211,8 +259,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       bool first = true;
       for (; it < seg_hi; ++it) {
-        uint64_t* ready = NORM ? &xready[stage] : &full[stage];
-        if (!mbar_wait(ready, phase, p.err, kDevErrFullWait)) {
+        if (!mbar_wait(&full[stage], phase, p.err, kDevErrFullWait)) {
           ok = false;
           break;
         }
@@ -225,15 +272,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t acc = (first && kk == 0) ? 0u : 1u;
             umma_bf16(tmem, da + 2 * kk, db + 2 * kk, idesc, acc);
-            if (SWIGLU) {
-              const uint64_t du = umma_desc_sw128(sb + WBOX);
-              umma_bf16(tmem + NMMA, du + 2 * kk, db + 2 * kk, idesc, acc);
-            }
-            if (NORM) {  // low part of x*gamma into the same accumulators
-              const uint64_t dl = umma_desc_sw128(sb + LY::XL_OFF);
-              umma_bf16(tmem, da + 2 * kk, dl + 2 * kk, idesc, 1u);
-              if (SWIGLU) umma_bf16(tmem + NMMA, umma_desc_sw128(sb + WBOX) + 2 * kk, dl + 2 * kk, idesc, 1u);
-            }
+            if (SWIGLU) umma_bf16(tmem + NMMA, umma_desc_sw128(sb + WBOX) + 2 * kk, db + 2 * kk, idesc, acc);
           }
           umma_commit(&empty[stage]);
         }
@@ -249,241 +288,262 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       __syncwarp();
       acc_phase ^= 1;
     }
-    if (!ok) *abort_sm = 1;
-  } else {
-    // ------------------------- transform + epilogue -------------------------
-    const int et = threadIdx.x - EPI_WARP0 * 32;  // 0..127
-    const int q = warp & 3;                       // TMEM lane quarter of this warp
-    const int row = 32 * q + lane;                // output feature within the row block
-    const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t acc_phase = 0;
-    long long it = it_begin;
-    bool ok = true;
-    while (ok && it < it_end) {
-      const int rb = (int)(it / p.KI);
-      const long long seg_lo = it;
-      const long long seg_hi = min(it_end, (long long)(rb + 1) * p.KI);
-      const bool full_rb = (seg_lo == (long long)rb * p.KI) && (seg_hi == (long long)(rb + 1) * p.KI);
-      float ss0 = 0.f, ss1 = 0.f;  // tokens et and et + 128
-      if (NORM) {
-        for (; it < seg_hi; ++it) {
-          if (!mbar_wait(&full[stage], phase, p.err, kDevErrFullWait)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + stage * LY::STAGE_BYTES;
-          const uint4* gam = reinterpret_cast<const uint4*>(st + LY::G_OFF);
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int tok = et + half * 128;
-            if (tok < NMMA) {  // rows >= M are TMA zero-fill: their lo part is written as zero too
-              uint4* xr = reinterpret_cast<uint4*>(st + LY::X_OFF + tok * 128);
-              uint4* xl = reinterpret_cast<uint4*>(st + LY::XL_OFF + tok * 128);
-              float ssl = 0.f;
-#pragma unroll
-              for (int pc = 0; pc < 8; ++pc) {
-                uint4 xv = xr[pc];
-                uint4 lv;
-                const uint4 gv = gam[pc ^ (tok & 7)];
-                uint32_t* xw = reinterpret_cast<uint32_t*>(&xv);
-                uint32_t* lw = reinterpret_cast<uint32_t*>(&lv);
-                const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[e]));
-                  const float2 gg = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
-                  ssl = fmaf(f.x, f.x, fmaf(f.y, f.y, ssl));
-                  const float p0 = f.x * gg.x, p1 = f.y * gg.y;
-                  const __nv_bfloat162 hi = __floats2bfloat162_rn(p0, p1);
-                  const float2 hf = __bfloat1622float2(hi);
-                  xw[e] = *reinterpret_cast<const uint32_t*>(&hi);
-                  lw[e] = pack_bf16x2(p0 - hf.x, p1 - hf.y);
-                }
-                xr[pc] = xv;
-                xl[pc] = lv;
-              }
-              if (half == 0) ss0 += ssl; else ss1 += ssl;
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&xready[stage]);
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
-        ss_sm[et] = ss0;
-        if (et + 128 < 256) ss_sm[et + 128] = ss1;
-      } else {
-        it = seg_hi;
-      }
-      named_bar_sync(1, EPI_THREADS);  // ss_sm complete
-
-      if (!mbar_wait(acc_full, acc_phase, p.err, kDevErrMmaWait)) {
-        ok = false;
-        break;
-      }
-      acc_phase ^= 1;
-      tc_fence_after();
-
-      const int col = rb * BM + row;
-      if (full_rb) {
-        for (int c0 = 0; c0 < NMMA && c0 < p.M; c0 += 16) {
-          float a[16], u[16];
-          tmem_ld16(trow + c0, a);
-          if (SWIGLU) tmem_ld16(trow + NMMA + c0, u);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int m = c0 + i;
-            if (m < p.M && col < p.N) {
-              float rs = 1.f;
-              if (NORM) rs = rsqrtf(ss_sm[m] * p.inv_k + p.eps);
-              float val = SWIGLU ? silu_f(a[i] * rs) * (u[i] * rs) : a[i] * rs;
-              const size_t off = (size_t)m * p.N + col;
-              if (p.residual) val += __bfloat162float(p.residual[off]);
-              p.y[off] = __float2bfloat16_rn(val);
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
-      } else {
-        const int slot = 2 * cta + (seg_lo == it_begin ? 0 : 1);
-        float* sp = p.partials + (size_t)slot * SLOT;
-        for (int c0 = 0; c0 < NMMA && c0 < p.M; c0 += 16) {
-          float a[16];
-          tmem_ld16(trow + c0, a);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) __stcg(sp + (size_t)(c0 + i) * BM + row, a[i]);
-          if (SWIGLU) {
-            tmem_ld16(trow + NMMA + c0, a);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) __stcg(sp + (size_t)NMMA * BM + (size_t)(c0 + i) * BM + row, a[i]);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
-        if (NORM) {
-          for (int m = et; m < NMMA; m += EPI_THREADS) __stcg(sp + (size_t)NMAT * NMMA * BM + m, ss_sm[m]);
-        }
-        __threadfence();
-        named_bar_sync(1, EPI_THREADS);
-        if (et == 0) {
-          const int cnt = (int)(seg_hi - seg_lo);
-          const int prev = atomicAdd(p.counters + rb, cnt);
-          const int last = (prev + cnt == p.KI);
-          if (last) p.counters[rb] = 0;
-          *flag_sm = last;
-        }
-        named_bar_sync(1, EPI_THREADS);
-        if (*flag_sm) {
-          __threadfence();
-          const long long lo = (long long)rb * p.KI, hi = lo + p.KI;
-          int cf = (int)(lo * p.G / p.total);
-          while (cf > 0 && it_start(p, cf) > lo) --cf;
-          while (it_start(p, cf + 1) <= lo) ++cf;
-          // total sum of squares per token (NORM), staged in ss_sm
-          if (NORM) {
-            named_bar_sync(1, EPI_THREADS);
-            for (int m = et; m < NMMA; m += EPI_THREADS) {
-              float s = 0.f;
-              for (int cc = cf; cc < p.G && it_start(p, cc) < hi; ++cc) {
-                if (it_start(p, cc + 1) == it_start(p, cc)) continue;
-                const int sl = 2 * cc + (it_start(p, cc) >= lo ? 0 : 1);
-                s += __ldcg(p.partials + (size_t)sl * SLOT + (size_t)NMAT * NMMA * BM + m);
-              }
-              ss_sm[m] = s;
-            }
-            named_bar_sync(1, EPI_THREADS);
-          }
-          // Sum the contributors' partials 16 tokens at a time: 16 (or 32)
-          // independent loads in flight per contributor keep this
-          // throughput-bound instead of latency-bound.
-          for (int c0 = 0; c0 < NMMA && c0 < p.M; c0 += 16) {
-            float g[16], u[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) g[i] = u[i] = 0.f;
-            for (int cc = cf; cc < p.G && it_start(p, cc) < hi; ++cc) {
-              if (it_start(p, cc + 1) == it_start(p, cc)) continue;
-              const int sl = 2 * cc + (it_start(p, cc) >= lo ? 0 : 1);
-              const float* qp = p.partials + (size_t)sl * SLOT + (size_t)c0 * BM + row;
-#pragma unroll
-              for (int i = 0; i < 16; ++i) g[i] += __ldcg(qp + i * BM);
-              if (SWIGLU) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) u[i] += __ldcg(qp + (size_t)NMMA * BM + i * BM);
-              }
-            }
-            if (col < p.N) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int m = c0 + i;
-                if (m < p.M) {
-                  float rs = 1.f;
-                  if (NORM) rs = rsqrtf(ss_sm[m] * p.inv_k + p.eps);
-                  float val = SWIGLU ? silu_f(g[i] * rs) * (u[i] * rs) : g[i] * rs;
-                  const size_t off = (size_t)m * p.N + col;
-                  if (p.residual) val += __bfloat162float(p.residual[off]);
-                  p.y[off] = __float2bfloat16_rn(val);
-                }
-              }
-            }
-          }
-        }
-      }
-      named_bar_sync(1, EPI_THREADS);  // ss_sm / flag reuse by the next segment
-    }
-    if (!ok) *abort_sm = 1;
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
+    // Free TMEM only after the epilogue warps have read their last accumulator.
+    mbar_wait(done, 0, p.err, kDevErrMmaWait);
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(LY::TMEM_COLS));
+    return;
+  }
+
+  // --------------------------------- epilogue ---------------------------------
+  const int et = threadIdx.x - EPI_WARP0 * 32;  // 0..127
+  const int q = warp & 3;                       // TMEM lane quarter of this warp
+  const int row = 32 * q + lane;                // output feature within the row block
+  const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // writes only after the previous kernel completed
+  uint32_t acc_phase = 0;
+  long long it = it_begin;
+  while (it < it_end) {
+    const int rb = (int)(it / p.KI);
+    const long long seg_lo = it;
+    const long long seg_hi = min(it_end, (long long)(rb + 1) * p.KI);
+    it = seg_hi;
+    const bool full_rb = (seg_lo == (long long)rb * p.KI) && (seg_hi == (long long)(rb + 1) * p.KI);
+    if (!mbar_wait(acc_full, acc_phase, p.err, kDevErrMmaWait)) break;
+    acc_phase ^= 1;
+    tc_fence_after();
+    if (et == 0) TC_TRACE(3 + 5 * (seg_lo != it_begin));
+    const int col = rb * BM + row;
+
+    if (full_rb) {
+      for (int c0 = 0; c0 < mcols; c0 += 16) {
+        float a[16], u[16];
+        load_tokens<NORM>(trow, c0, p.Mp, a);
+        if (SWIGLU) load_tokens<NORM>(trow + NMMA, c0, p.Mp, u);
+        if (col < p.N) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < p.M) store_out(p, c0 + i, col, a[i], SWIGLU ? u[i] : 0.f, SWIGLU);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      continue;
+    }
+
+    // Partial row block: [matrix][row][NMMA] fp32, 16 tokens (64 B) per thread per chunk.
+    const int slot = 2 * cta + (seg_lo == it_begin ? 0 : 1);
+    float* sp = p.partials + (size_t)slot * SLOT;
+    for (int c0 = 0; c0 < mcols; c0 += 16) {
+      float a[16];
+      load_tokens<NORM>(trow, c0, p.Mp, a);
+      float4* d = reinterpret_cast<float4*>(sp + (size_t)row * NMMA + c0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) __stcg(d + i, make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]));
+      if (SWIGLU) {
+        load_tokens<NORM>(trow + NMMA, c0, p.Mp, a);
+        d = reinterpret_cast<float4*>(sp + (size_t)NMMA * BM + (size_t)row * NMMA + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) __stcg(d + i, make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]));
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(acc_empty);  // the MMA warp may start the next segment
+    if (et == 0) TC_TRACE(5 + 5 * (seg_lo != it_begin));
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(done);
+  if (et == 0) TC_TRACE(12);
+}
+
+// RMSNorm prologue: one CTA per token row m < Mp. rstd[m] = rsqrt(mean(x^2) + eps);
+// xs[m] = bf16(x*gamma), xs[Mp + m] = bf16(x*gamma - xs[m]); rows m >= M are zero.
+__global__ void __launch_bounds__(256) rms_split_kernel(const __nv_bfloat16* __restrict__ x,
+                                                        const __nv_bfloat16* __restrict__ gamma, float eps, int K,
+                                                        int M, int Mp, __nv_bfloat16* __restrict__ xs,
+                                                        float* __restrict__ rstd) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // let the GEMM start streaming W
+  const int m = blockIdx.x;
+  uint4* hi = reinterpret_cast<uint4*>(xs + (size_t)m * K);
+  uint4* lo = reinterpret_cast<uint4*>(xs + (size_t)(Mp + m) * K);
+  const int nv = K / 8;
+  if (m >= M) {
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) hi[i] = lo[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) rstd[m] = 0.f;
+    return;
+  }
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)m * K);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    const uint4 xv = __ldg(xr + i);
+    const uint4 gv = __ldg(gr + i);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+    uint4 hv, lv;
+    uint32_t* hw = reinterpret_cast<uint32_t*>(&hv);
+    uint32_t* lw = reinterpret_cast<uint32_t*>(&lv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[e]));
+      const float2 gg = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      const float p0 = f.x * gg.x, p1 = f.y * gg.y;
+      const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+      const float2 hf = __bfloat1622float2(h);
+      hw[e] = *reinterpret_cast<const uint32_t*>(&h);
+      lw[e] = pack_bf16x2(p0 - hf.x, p1 - hf.y);
+    }
+    hi[i] = hv;
+    lo[i] = lv;
+  }
+  __shared__ float red[8];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    rstd[m] = rsqrtf(t / (float)K + eps);
   }
 }
 
+
+// Split row blocks: sum the contributors' fp32 partials (in contributor order,
+// deterministic) and apply the epilogue. Grid (row block, 16-token chunk),
+// 128 threads = the block's 128 output features; row blocks finished inside
+// one CTA of the GEMM were already written and exit here at once. Launched as
+// a programmatic dependent of the GEMM: griddepcontrol.wait returns once the
+// GEMM grid has completed and its writes are visible.
+template <int NMMA, bool SWIGLU>
+__global__ void __launch_bounds__(128) tc_reduce_kernel(Params p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int rb = blockIdx.x;
+  const int c0 = blockIdx.y * 8;
+  const long long lo = (long long)rb * p.KI, hi = lo + p.KI;
+  int cf = (int)((double)lo * p.G / (double)p.total);
+  if (cf > p.G - 1) cf = p.G - 1;
+  while (cf > 0 && it_start(p, cf) > lo) --cf;
+  while (it_start(p, cf + 1) <= lo) ++cf;
+  if (it_start(p, cf) <= lo && it_start(p, cf + 1) >= hi) return;  // whole block inside one CTA
+  int cl = cf;
+  while (cl + 1 < p.G && it_start(p, cl + 1) < hi) ++cl;  // last contributor
+  constexpr int SLOT = slot_floats(NMMA, SWIGLU);
+  const int row = threadIdx.x;
+  const size_t roff = (size_t)row * NMMA + c0;
+  float4 g[2], u[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) g[i] = u[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Four contributors per batch: all their loads are in flight before the adds
+  // (which stay in contributor order).
+  for (int cb = cf; cb <= cl; cb += 4) {
+    float4 tg[4][2], tu[4][2];
+    bool use[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int cc = cb + k;
+      use[k] = cc <= cl && it_start(p, cc + 1) != it_start(p, cc);
+      const int sl = use[k] ? 2 * cc + (it_start(p, cc) >= lo ? 0 : 1) : 0;
+      const float4* base = reinterpret_cast<const float4*>(p.partials + (size_t)sl * SLOT + roff);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) tg[k][i] = use[k] ? __ldcg(base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (SWIGLU) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          tu[k][i] = use[k] ? __ldcg(base + (size_t)NMMA * BM / 4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (!use[k]) continue;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        g[i].x += tg[k][i].x; g[i].y += tg[k][i].y; g[i].z += tg[k][i].z; g[i].w += tg[k][i].w;
+        if (SWIGLU) {
+          u[i].x += tu[k][i].x; u[i].y += tu[k][i].y; u[i].z += tu[k][i].z; u[i].w += tu[k][i].w;
+        }
+      }
+    }
+  }
+  const int col = rb * BM + row;
+  if (col >= p.N) return;
+  const float* gf = reinterpret_cast<const float*>(g);
+  const float* uf = reinterpret_cast<const float*>(u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (c0 + i < p.M) store_out(p, c0 + i, col, gf[i], uf[i], SWIGLU);
+}
+
 template <int NMMA, bool SWIGLU, bool NORM>
-static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtensorMap& tmX, const CUtensorMap& tmG,
-                  const Params& p, cudaStream_t stream) {
-  using LY = Layout<NMMA, SWIGLU, NORM>;
+static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtensorMap& tmX, const Params& p,
+                  cudaStream_t stream) {
+  using LY = Layout<NMMA, SWIGLU>;
   static_assert(LY::STAGES >= 2, "stage does not fit");
   auto kern = gemm_tc_kernel<NMMA, SWIGLU, NORM>;
   FK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LY::SMEM));
-  kern<<<p.G, NTHREADS, LY::SMEM, stream>>>(tmW, tmWu, tmX, tmG, p);
-  FK_CHECK_CUDA(cudaGetLastError());
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    cudaLaunchConfig_t g = {};
+    g.gridDim = dim3((unsigned)p.G, 1, 1);
+    g.blockDim = dim3(NTHREADS, 1, 1);
+    g.dynamicSmemBytes = LY::SMEM;
+    g.stream = stream;
+    g.attrs = attr;
+    g.numAttrs = 1;
+    FK_CHECK_CUDA(cudaLaunchKernelEx(&g, kern, tmW, tmWu, tmX, p));
+  }
+  // Reduction of split row blocks, as a programmatic dependent launch.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.num_rb, (unsigned)((p.M + 7) / 8), 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, tc_reduce_kernel<NMMA, SWIGLU>, p));
   return kOk;
 }
 
 template <bool SWIGLU, bool NORM>
-static int launch_n(int nmma, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
-                    const Params& p, cudaStream_t st) {
+static int launch_n(int nmma, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const Params& p,
+                    cudaStream_t st) {
   switch (nmma) {
-    case 32: return launch<32, SWIGLU, NORM>(a, b, c, d, p, st);
-    case 64: return launch<64, SWIGLU, NORM>(a, b, c, d, p, st);
-    case 128: return launch<128, SWIGLU, NORM>(a, b, c, d, p, st);
-    case 256: return launch<256, SWIGLU, NORM>(a, b, c, d, p, st);
+    case 32: return launch<32, SWIGLU, NORM>(a, b, c, p, st);
+    case 64: return launch<64, SWIGLU, NORM>(a, b, c, p, st);
+    case 128: return launch<128, SWIGLU, NORM>(a, b, c, p, st);
+    case 256: return launch<256, SWIGLU, NORM>(a, b, c, p, st);
     default: return fail(kErrUnsupported, "unsupported token tile");
   }
 }
 
-// Token tile: the smallest of {32, 64, 128, 256} covering M (capped at 256).
-static int token_tile(int M) { return M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
+// Token tile: the smallest of {32, 64, 128, 256} covering n columns.
+static int token_tile(int n) { return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : 256; }
+static int round16(int n) { return (n + 15) / 16 * 16; }
+
+// Largest token tile any launch of a call with M tokens uses (plain or RMSNorm).
+static int max_tile(int M) {
+  const int plain = token_tile(M < 256 ? M : 256);
+  const int mt = M < NORM_TILE ? M : NORM_TILE;
+  const int norm = token_tile(2 * round16(mt));
+  return plain > norm ? plain : norm;
+}
 
 }  // namespace tc
 
+// Workspace: [16 KB header (unused here)][RMSNorm split x: 2*128*K bf16][rstd: 128 fp32][partials].
+static size_t tc_xs_bytes(int K) { return ((size_t)2 * tc::NORM_TILE * K * 2 + 255) / 256 * 256; }
+static size_t tc_rstd_bytes() { return 512; }
+
 size_t tc_workspace_bytes(int M, int N, int K, bool swiglu) {
-  (void)K;
-  const int num_rb = (N + tc::BM - 1) / tc::BM;
-  (void)num_rb;
-  return kCounterBytes + (size_t)2 * num_sms() * tc::slot_floats(tc::token_tile(M), swiglu) * 4;
+  (void)N;
+  return kCounterBytes + tc_xs_bytes(K) + tc_rstd_bytes() +
+         (size_t)2 * num_sms() * tc::slot_floats(tc::max_tile(M), swiglu) * 4;
 }
 
 int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
@@ -503,12 +563,13 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   int* err = device_error_word();
   if (!err) return fail(kErrCuda, "device error word unavailable");
 
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ws + kCounterBytes);
+  float* rstd = reinterpret_cast<float*>(ws + kCounterBytes + tc_xs_bytes(K));
   const int num_rb = (N + tc::BM - 1) / tc::BM;
   const int KI = (K + tc::BK - 1) / tc::BK;
   tc::Params p;
-  p.residual = static_cast<const __nv_bfloat16*>(residual);
-  p.counters = static_cast<int*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
+  p.partials = reinterpret_cast<float*>(ws + kCounterBytes + tc_xs_bytes(K) + tc_rstd_bytes());
   p.err = err;
   p.N = N;
   p.K = K;
@@ -516,13 +577,14 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   p.num_rb = num_rb;
   p.up_row_offset = up_row_offset;
   p.total = (long long)num_rb * KI;
+  FK_CHECK_ARG(p.total < (1LL << 31), "problem too large for the iteration table");
   int G = num_sms();
+  if (G > tc::kMaxGrid) G = tc::kMaxGrid;
   if ((long long)G > p.total) G = (int)p.total;
   p.G = G;
-  p.eps = eps;
-  p.inv_k = 1.f / (float)K;
+  for (int c = 0; c <= G; ++c) p.starts[c] = (int)((long long)c * p.total / G);
 
-  CUtensorMap tmW, tmWu, tmG;
+  CUtensorMap tmW, tmWu;
   const uint64_t strides[1] = {(uint64_t)K * 2};
   const uint32_t wbox[2] = {64, (uint32_t)tc::BM};
   const uint64_t wdims[2] = {(uint64_t)K, (uint64_t)(sw && w_up == w ? up_row_offset + N : N)};
@@ -537,40 +599,55 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   } else {
     tmWu = tmW;
   }
-  if (norm) {
-    const uint64_t gdims[1] = {(uint64_t)K};
-    const uint32_t gbox[1] = {(uint32_t)tc::BK};
-    rc = encode_tma(&tmG, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 1, const_cast<void*>(gamma), gdims, nullptr, gbox,
-                    CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
-  } else {
-    tmG = tmW;
-  }
-  // Token tiles of up to 256: one launch per tile, in order on the stream.
-  for (int m0 = 0; m0 < M; m0 += 256) {
-    const int mt = M - m0 < 256 ? M - m0 : 256;
-    const int nmma = tc::token_tile(mt);
+  // Token tiles: one launch per tile, in order on the stream (RMSNorm: 128 tokens
+  // per tile, each preceded by its split prologue).
+  const int tile = norm ? tc::NORM_TILE : 256;
+  for (int m0 = 0; m0 < M; m0 += tile) {
+    const int mt = M - m0 < tile ? M - m0 : tile;
+    const __nv_bfloat16* xt = static_cast<const __nv_bfloat16*>(x) + (size_t)m0 * K;
     CUtensorMap tmX;
-    const uint64_t xdims[2] = {(uint64_t)K, (uint64_t)mt};
+    int nmma, xrows;
+    const void* xsrc;
+    if (norm) {
+      const int Mp = tc::round16(mt);
+      tc::rms_split_kernel<<<Mp, 256, 0, stream>>>(xt, static_cast<const __nv_bfloat16*>(gamma), eps, K, mt, Mp, xs,
+                                                   rstd);
+      FK_CHECK_CUDA(cudaGetLastError());
+      p.Mp = Mp;
+      p.rstd = rstd;
+      xrows = 2 * Mp;
+      nmma = tc::token_tile(2 * Mp);
+      xsrc = xs;
+    } else {
+      p.Mp = 0;
+      p.rstd = nullptr;
+      xrows = mt;
+      nmma = tc::token_tile(mt);
+      xsrc = xt;
+    }
+    const uint64_t xdims[2] = {(uint64_t)K, (uint64_t)xrows};
     const uint32_t xbox[2] = {64, (uint32_t)nmma};
-    rc = encode_tma(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                    const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)) + (size_t)m0 * K, xdims, strides,
-                    xbox, CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = encode_tma(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(xsrc), xdims, strides, xbox,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     p.M = mt;
     p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * N;
     p.residual = residual ? static_cast<const __nv_bfloat16*>(residual) + (size_t)m0 * N : nullptr;
-    if (!norm) tmG = tmX;
-    if (sw) {
-      rc = norm ? tc::launch_n<true, true>(nmma, tmW, tmWu, tmX, tmG, p, stream)
-                : tc::launch_n<true, false>(nmma, tmW, tmWu, tmX, tmG, p, stream);
-    } else {
-      rc = norm ? tc::launch_n<false, true>(nmma, tmW, tmWu, tmX, tmG, p, stream)
-                : tc::launch_n<false, false>(nmma, tmW, tmWu, tmX, tmG, p, stream);
-    }
+    if (sw)
+      rc = norm ? tc::launch_n<true, true>(nmma, tmW, tmWu, tmX, p, stream)
+                : tc::launch_n<true, false>(nmma, tmW, tmWu, tmX, p, stream);
+    else
+      rc = norm ? tc::launch_n<false, true>(nmma, tmW, tmWu, tmX, p, stream)
+                : tc::launch_n<false, false>(nmma, tmW, tmWu, tmX, p, stream);
     if (rc) return rc;
   }
   return kOk;
 }
 
 }  // namespace fk
+
+#ifdef FK_TC_TRACE
+extern "C" int fk_tc_trace_dump(unsigned long long* host, int n) {
+  return cudaMemcpyFromSymbol(host, fk::tc::g_tc_trace, sizeof(unsigned long long) * n) == cudaSuccess ? 0 : -3;
+}
+#endif

@@ -75,7 +75,19 @@ def case_tc_m128_swiglu(launches: int):
     _gemm_case(128, 14336, 4096, launches, "swiglu")
 
 
+def case_tc_m64(launches: int):
+    """tcgen05 GEMM, config 3 at M=64."""
+    _gemm_case(64, 14336, 4096, launches)
+
+
+def case_tc_m128_rms_qkv(launches: int):
+    """tcgen05 RMSNorm->QKV GEMM, config 4 at M=128: W [6144, 4096] = 50 MB."""
+    _gemm_case(128, 6144, 4096, launches, "rms")
+
+
 CASES = {
+    "tc_m64": case_tc_m64,
+    "tc_m128_rms_qkv": case_tc_m128_rms_qkv,
     "attn_small": case_attn_small,
     "skinny_m16": case_skinny_m16,
     "skinny_m1": case_skinny_m1,
