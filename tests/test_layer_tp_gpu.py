@@ -1,0 +1,73 @@
+"""Tensor-parallel decode step on 2 GPUs (NCCL) against the single-GPU layer and the oracle."""
+import datetime
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+needs_2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                             reason="needs 2 GPUs")
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+
+        import oracle
+        from fused_kernels_cutedsl_lib_b200 import _native
+        from fused_kernels_cutedsl_lib_b200.layer import TPDecodeLayer, random_layer_weights, shard_layer_weights
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        B, L, H, F, HQ, HKV = 16, 300, 4096, 14336, 32, 8
+        full = random_layer_weights(H, F, HQ, HKV, seed=11, device=dev)
+        g = torch.Generator(device=dev).manual_seed(12)
+        x = torch.randn(B, H, generator=g, device=dev).bfloat16()
+        k = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
+        v = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
+        lens = torch.tensor([250 + 3 * i for i in range(B)], dtype=torch.int32, device=dev)
+        ref, *_ = oracle.decode_layer(x, full.as_dict(), k, v, lens, num_heads_q=HQ, num_heads_kv=HKV)
+        Bl = B // world
+        rows = slice(rank * Bl, (rank + 1) * Bl)
+        layer = TPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
+        kr, vr, lr = k[rows].contiguous(), v[rows].contiguous(), lens[rows].contiguous()
+        y = layer(x, kr, vr, lr)
+        torch.cuda.synchronize()
+        err = ((y.float().cpu() - ref).abs() / ref.abs().clamp_min(1.0))
+        q.put((rank, err.max().item(), err.mean().item(), lr.cpu().tolist(), _native.device_error()))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e), None, None, None))
+
+
+@needs_2
+def test_tp2_layer_matches_oracle():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r[0]: r for r in (q.get(timeout=300) for _ in procs)}
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        _, mx, mean, lens, derr = res[r]
+        assert not isinstance(mx, str), mx
+        assert derr == 0
+        assert mx <= 5e-2 and mean <= 1e-2, (mx, mean)  # chained bound, as for the single-GPU layer
+        assert lens == [251 + 3 * i for i in range(r * 8, r * 8 + 8)]
