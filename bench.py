@@ -367,7 +367,7 @@ def run_layer(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     B, ctx, H, F, HQ, HKV = 128, 8192, 4096, 14336, 32, 8
-    Lmax = ctx + args.warmup + 2 * args.steps + 16
+    Lmax = ctx + args.warmup + 2 * args.steps + 32
     full = random_layer_weights(H, F, HQ, HKV, seed=4, device=dev)
     Bl = B // world
     g = torch.Generator(device=dev).manual_seed(4 * 1000 + rank)
@@ -386,6 +386,33 @@ def run_layer(args):
     for _ in range(args.warmup):
         layer(x, k, v, lens)
     torch.cuda.synchronize()
+    x_h = x.cpu().pin_memory()
+    y_h = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x)
+    step, step_e2e = (lambda: layer(x, k, v, lens)), None
+
+    def e2e_body():
+        x_d.copy_(x_h, non_blocking=True)
+        y_h.copy_(layer(x_d, k, v, lens), non_blocking=True)
+
+    step_e2e = e2e_body
+    # Graph capture is used on one GPU only: a capture of the tensor-parallel step
+    # (NCCL all-gathers interleaved with programmatic-dependent launches) did not
+    # complete on the GPU box, so N > 1 launches eagerly until that is resolved.
+    use_graph = not args.no_graph and world == 1
+    if use_graph:
+        # One decode step (7 launches on 1 GPU; + 5 all-gathers under TP) captured
+        # once and replayed: no per-launch host work inside the timed loop.
+        g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            layer(x, k, v, lens)
+        with torch.cuda.graph(g2):
+            e2e_body()
+        torch.cuda.synchronize()
+        step, step_e2e = g1.replay, g2.replay
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
@@ -393,7 +420,7 @@ def run_layer(args):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     for _ in range(args.steps):
-        layer(x, k, v, lens)
+        step()
     b.record(stream)
     torch.cuda.synchronize()
     clocks.mark_end()
@@ -402,15 +429,10 @@ def run_layer(args):
     if _native.device_error() != 0:
         raise RuntimeError("device error word set during the bench")
     # e2e: x H2D from pinned host, y D2H, inside the timed region
-    x_h = x.cpu().pin_memory()
-    y_h = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
-    x_d = torch.empty_like(x)
     a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a2.record(stream)
     for _ in range(args.steps):
-        x_d.copy_(x_h, non_blocking=True)
-        y = layer(x_d, k, v, lens)
-        y_h.copy_(y, non_blocking=True)
+        step_e2e()
     b2.record(stream)
     torch.cuda.synchronize()
     e2e_ms = a2.elapsed_time(b2) / args.steps
@@ -429,6 +451,7 @@ def run_layer(args):
             "config": {"workload": "decode_layer_config5", "batch": B, "context": ctx, "hidden": H, "ffn": F,
                        "heads_q": HQ, "heads_kv": HKV,
                        "parallelism": "single GPU" if world == 1 else f"tp{world} GEMMs + batch-sharded attention",
+                       "cuda_graph": (not args.no_graph) and world == 1,
                        "l2": "weights 436 MB + KV 4.3 GB per step exceed L2"},
             "bytes_per_step": wbytes + kv_bytes,
             "achieved_TBps": round((wbytes + kv_bytes) / world / (ms * 1e-3) / 1e12, 3),
@@ -451,6 +474,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="layer workload: launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--workload", choices=["attention", "layer"], default="attention",
                     help="attention: config 2 split-KV decode attention (headline); layer: config 5 decode step")
     args = ap.parse_args()

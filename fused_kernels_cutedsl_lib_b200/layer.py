@@ -158,13 +158,9 @@ class KernelOps:
 
     def __init__(self, num_heads_q, num_heads_kv, eps):
         self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
-        self._ws: dict = {}
 
     def _wsp(self, x):
-        key = str(x.device)
-        if key not in self._ws:
-            self._ws[key] = alloc_workspace(64 << 20, x.device)
-        return self._ws[key]
+        return None  # the per-device shared workspace of gemm.linear, grown on demand
 
     def rms_linear(self, x, gamma, w, out):
         return linear(x, w, out, gamma=gamma, eps=self.eps, workspace=self._wsp(x))
