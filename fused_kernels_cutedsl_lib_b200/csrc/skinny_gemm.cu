@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   __syncthreads();
 
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   if (warp == NCW) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
@@ -127,30 +129,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (NORM) tma_prefetch_desc(&tmG);
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      for (long long it = it_begin; it < it_end; ++it) {
+      auto load_w = [&](int s, long long it) {
         const int rb = (int)(it / p.KI);
         const int k0 = (int)(it - (long long)rb * p.KI) * KT;
-        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) return;
-        uint8_t* st = smem + stage * LY::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[stage], LY::TX_BYTES);
-        tma_load_2d(st, &tmW, &full[stage], k0, rb * RB, pol_w);
-        tma_load_2d(st + WBOX_BYTES, &tmW, &full[stage], k0 + 64, rb * RB, pol_w);
+        uint8_t* st = smem + s * LY::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], LY::TX_BYTES);
+        tma_load_2d(st, &tmW, &full[s], k0, rb * RB, pol_w);
+        tma_load_2d(st + WBOX_BYTES, &tmW, &full[s], k0 + 64, rb * RB, pol_w);
         if (SWIGLU) {
-          tma_load_2d(st + WTILE_BYTES, &tmWu, &full[stage], k0, p.up_row_offset + rb * RB, pol_w);
-          tma_load_2d(st + WTILE_BYTES + WBOX_BYTES, &tmWu, &full[stage], k0 + 64,
-                      p.up_row_offset + rb * RB, pol_w);
+          tma_load_2d(st + WTILE_BYTES, &tmWu, &full[s], k0, p.up_row_offset + rb * RB, pol_w);
+          tma_load_2d(st + WTILE_BYTES + WBOX_BYTES, &tmWu, &full[s], k0 + 64, p.up_row_offset + rb * RB, pol_w);
         }
-        tma_load_2d(st + LY::X_OFF, &tmX, &full[stage], k0, 0, pol_x);
-        tma_load_2d(st + LY::X_OFF + LY::XBOX_BYTES, &tmX, &full[stage], k0 + 64, 0, pol_x);
+      };
+      auto load_x = [&](int s, long long it) {
+        const int k0 = (int)(it % p.KI) * KT;
+        uint8_t* st = smem + s * LY::STAGE_BYTES;
+        tma_load_2d(st + LY::X_OFF, &tmX, &full[s], k0, 0, pol_x);
+        tma_load_2d(st + LY::X_OFF + LY::XBOX_BYTES, &tmX, &full[s], k0 + 64, 0, pol_x);
         if (NORM) {
           asm volatile(
               "cp.async.bulk.tensor.1d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
               " [%0], [%1, {%2}], [%3], %4;" ::"r"(smem_u32(st + LY::G_OFF)),
-              "l"(reinterpret_cast<uint64_t>(&tmG)), "r"(k0), "r"(smem_u32(&full[stage])), "l"(pol_x)
+              "l"(reinterpret_cast<uint64_t>(&tmG)), "r"(k0), "r"(smem_u32(&full[s])), "l"(pol_x)
               : "memory");
         }
+      };
+      // Weights never depend on the previous kernel on the stream: the first
+      // ring of W tiles is requested before waiting for it (programmatic
+      // dependent launch); x (the previous kernel's output) only after.
+      const long long pre_end = it_begin + STAGES < it_end ? it_begin + STAGES : it_end;
+      for (long long it = it_begin; it < pre_end; ++it) load_w((int)(it - it_begin), it);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (long long it = it_begin; it < pre_end; ++it) load_x((int)(it - it_begin), it);
+      int stage = (int)((pre_end - it_begin) % STAGES);
+      uint32_t phase = (pre_end - it_begin) >= STAGES ? 1u : 0u;
+      for (long long it = pre_end; it < it_end; ++it) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) return;
+        load_w(stage, it);
+        load_x(stage, it);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
@@ -166,6 +182,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int j = lane >> 3;
   const int r = lane & 7;
   const int ctid = threadIdx.x;  // 0..255
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // writes only after the previous kernel completed
   int stage = 0;
   uint32_t phase = 0;
 
@@ -404,7 +421,19 @@ static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtenso
   static_assert(LY::STAGES >= 2, "stage does not fit");
   auto kern = skinny_gemm_kernel<NT, SWIGLU, NORM>;
   FK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LY::SMEM));
-  kern<<<p.G, NTHREADS, LY::SMEM, stream>>>(tmW, tmWu, tmX, tmG, p);
+  // Programmatic dependent launch: the weight stream of this GEMM may start
+  // while the previous kernel on the stream drains (see the producer).
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.G, 1, 1);
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = LY::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tmW, tmWu, tmX, tmG, p));
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
 }

@@ -66,6 +66,28 @@ def time_launches(fn, iters: int = 30, warmup: int = 3, flush: L2Flusher | None 
     return times
 
 
+def time_back_to_back(fn, n: int = 24, busy_cycles: int = 2_000_000) -> float:
+    """Average device time (ms) per call of ``n`` calls issued back to back.
+
+    This is the steady state of a decode step, where each GEMM follows another
+    kernel on the stream and its weight stream may start while that kernel
+    drains (programmatic dependent launch). A ~1 ms device spin queued first
+    lets the host enqueue every call before the first one starts.
+    """
+    stream = torch.cuda.current_stream()
+    fn(0)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(busy_cycles)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(n):
+        fn(i)
+    b.record(stream)
+    b.synchronize()
+    return a.elapsed_time(b) / n
+
+
 def weight_copies(w: torch.Tensor, min_total: int = 320 << 20) -> list[torch.Tensor]:
     """``w`` plus clones so that the copies together exceed ``min_total`` bytes (>= 2 copies)."""
     nb = w.numel() * w.element_size()
@@ -102,13 +124,16 @@ def gemm_sweep(iters: int = 30, include_cublas: bool = True) -> list[dict]:
                 linear(x, wi, y, gamma=gamma, eps=1e-6, workspace=ws)
 
         t = statistics.median(time_launches(ours, iters))
+        tb = time_back_to_back(ours)
         nbytes = rows_w * K * 2 + M * K * 2 + M * N * 2 + (K * 2 if gamma is not None else 0)
         flops = 2 * M * rows_w * K
         row = {"kernel": kind, "M": M, "N": N, "K": K, "us": round(t * 1e3, 2),
                "TBps": round(nbytes / (t * 1e-3) / 1e12, 3),
                "hbm_frac": round(nbytes / (t * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
                "TFLOPs": round(flops / (t * 1e-3) / 1e12, 1),
-               "path": "stream-K mma.sync" if M <= 16 else "tcgen05/TMEM"}
+               "path": "stream-K mma.sync" if M <= 16 else "tcgen05/TMEM",
+               "us_back_to_back": round(tb * 1e3, 2),
+               "hbm_frac_back_to_back": round(nbytes / (tb * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)}
         if include_cublas:
             if sw:
                 def ref(i):
@@ -121,6 +146,7 @@ def gemm_sweep(iters: int = 30, include_cublas: bool = True) -> list[dict]:
                 def ref(i):
                     x @ ws_list[i % nw].t()
             tr = statistics.median(time_launches(ref, iters))
+            row["torch_us_back_to_back"] = round(time_back_to_back(ref) * 1e3, 2)
             row["torch_us"] = round(tr * 1e3, 2)
             row["speedup_vs_torch"] = round(tr / t, 2)
         row["weight_copies"] = nw
