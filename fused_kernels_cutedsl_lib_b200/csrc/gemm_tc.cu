@@ -332,20 +332,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       continue;
     }
 
-    // Partial row block: [matrix][row][NMMA] fp32, 16 tokens (64 B) per thread per chunk.
+    // Partial row block: [matrix][token][row] fp32 — a warp's store of one token
+    // is 128 contiguous bytes, and so is the reduction kernel's load.
     const int slot = 2 * cta + (seg_lo == it_begin ? 0 : 1);
-    float* sp = p.partials + (size_t)slot * SLOT;
+    float* sp = p.partials + (size_t)slot * SLOT + row;
     for (int c0 = 0; c0 < mcols; c0 += 16) {
       float a[16];
       load_tokens<NORM>(trow, c0, p.Mp, a);
-      float4* d = reinterpret_cast<float4*>(sp + (size_t)row * NMMA + c0);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) __stcg(d + i, make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]));
+      for (int i = 0; i < 16; ++i) __stcg(sp + (size_t)(c0 + i) * BM, a[i]);
       if (SWIGLU) {
         load_tokens<NORM>(trow + NMMA, c0, p.Mp, a);
-        d = reinterpret_cast<float4*>(sp + (size_t)NMMA * BM + (size_t)row * NMMA + c0);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) __stcg(d + i, make_float4(a[4 * i], a[4 * i + 1], a[4 * i + 2], a[4 * i + 3]));
+        for (int i = 0; i < 16; ++i) __stcg(sp + (size_t)NMMA * BM + (size_t)(c0 + i) * BM, a[i]);
       }
     }
     tc_fence_before();
@@ -434,48 +433,43 @@ __global__ void __launch_bounds__(128) tc_reduce_kernel(Params p) {
   while (cl + 1 < p.G && it_start(p, cl + 1) < hi) ++cl;  // last contributor
   constexpr int SLOT = slot_floats(NMMA, SWIGLU);
   const int row = threadIdx.x;
-  const size_t roff = (size_t)row * NMMA + c0;
-  float4 g[2], u[2];
+  const size_t roff = (size_t)c0 * BM + row;  // token c0, this feature row; next token +BM
+  float g[8], u[8];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) g[i] = u[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < 8; ++i) g[i] = u[i] = 0.f;
   // Four contributors per batch: all their loads are in flight before the adds
   // (which stay in contributor order).
   for (int cb = cf; cb <= cl; cb += 4) {
-    float4 tg[4][2], tu[4][2];
+    float tg[4][8], tu[4][8];
     bool use[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int cc = cb + k;
       use[k] = cc <= cl && it_start(p, cc + 1) != it_start(p, cc);
       const int sl = use[k] ? 2 * cc + (it_start(p, cc) >= lo ? 0 : 1) : 0;
-      const float4* base = reinterpret_cast<const float4*>(p.partials + (size_t)sl * SLOT + roff);
+      const float* base = p.partials + (size_t)sl * SLOT + roff;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) tg[k][i] = use[k] ? __ldcg(base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < 8; ++i) tg[k][i] = use[k] ? __ldcg(base + i * BM) : 0.f;
       if (SWIGLU) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
-          tu[k][i] = use[k] ? __ldcg(base + (size_t)NMMA * BM / 4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < 8; ++i) tu[k][i] = use[k] ? __ldcg(base + (size_t)NMMA * BM + i * BM) : 0.f;
       }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       if (!use[k]) continue;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        g[i].x += tg[k][i].x; g[i].y += tg[k][i].y; g[i].z += tg[k][i].z; g[i].w += tg[k][i].w;
-        if (SWIGLU) {
-          u[i].x += tu[k][i].x; u[i].y += tu[k][i].y; u[i].z += tu[k][i].z; u[i].w += tu[k][i].w;
-        }
+      for (int i = 0; i < 8; ++i) {
+        g[i] += tg[k][i];
+        if (SWIGLU) u[i] += tu[k][i];
       }
     }
   }
   const int col = rb * BM + row;
   if (col >= p.N) return;
-  const float* gf = reinterpret_cast<const float*>(g);
-  const float* uf = reinterpret_cast<const float*>(u);
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    if (c0 + i < p.M) store_out(p, c0 + i, col, gf[i], uf[i], SWIGLU);
+    if (c0 + i < p.M) store_out(p, c0 + i, col, g[i], u[i], SWIGLU);
 }
 
 template <int NMMA, bool SWIGLU, bool NORM>
