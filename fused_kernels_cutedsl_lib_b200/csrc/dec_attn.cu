@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   Walker w;
   w.init(p);
+  // Pass 2 may be scheduled now; it waits for this grid's completion itself.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == NCW) {
     // ------------------------------ producer ------------------------------
@@ -332,6 +334,8 @@ __global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ 
                                                       __nv_bfloat16* __restrict__ out,
                                                       float* __restrict__ lse, int B, int Hq,
                                                       int Lmax, int chunk) {
+  // Launched as a programmatic dependent of pass 1: wait for its partials.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= B * Hq) return;
@@ -503,9 +507,18 @@ int fk_dec_attn_combine(const float* o_partial, const float* lse_partial,
                "o_partial must be 16-byte and out 8-byte aligned");
   const int rows = batch * num_heads_q;
   const int chunk = attn::chunk_tokens(max_seqlen, num_splits);
-  attn::combine_kernel<<<(rows + 3) / 4, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      o_partial, lse_partial, cache_seqlens, static_cast<__nv_bfloat16*>(out), lse, batch,
-      num_heads_q, max_seqlen, chunk);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((rows + 3) / 4), 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn::combine_kernel, o_partial, lse_partial, cache_seqlens,
+                                   static_cast<__nv_bfloat16*>(out), lse, batch, num_heads_q, max_seqlen,
+                                   chunk));
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
 }
