@@ -19,6 +19,8 @@ from .gemm import (
     workspace_bytes,
 )
 from .decoding_attention import (
+    DAttn1,
+    DAttn2,
     DecodeAttention,
     alloc_partials,
     chunk_tokens,
@@ -42,6 +44,8 @@ __all__ = [
     "swiglu_gemm",
     "swiglu_gemm2",
     "workspace_bytes",
+    "DAttn1",
+    "DAttn2",
     "DecodeAttention",
     "alloc_partials",
     "chunk_tokens",

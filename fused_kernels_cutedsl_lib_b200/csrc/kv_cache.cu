@@ -56,3 +56,41 @@ extern "C" int fk_kv_append(const void* src, long long src_row_stride, int k_col
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
 }
+
+namespace fk {
+namespace kv {
+
+// Head-major scatter of a projection output: dst[h][row0 + m][d] = src[m][h*D + d].
+__global__ void __launch_bounds__(128) head_scatter_kernel(const __nv_bfloat16* __restrict__ q_src,
+                                                           const __nv_bfloat16* __restrict__ k_src,
+                                                           const __nv_bfloat16* __restrict__ v_src,
+                                                           __nv_bfloat16* __restrict__ q_out,
+                                                           __nv_bfloat16* __restrict__ k_cache,
+                                                           __nv_bfloat16* __restrict__ v_cache, int M, int H, int D,
+                                                           int P) {
+  const int m = blockIdx.x, h = blockIdx.y, which = blockIdx.z;
+  const __nv_bfloat16* src = which == 0 ? q_src : which == 1 ? k_src : v_src;
+  __nv_bfloat16* dst = which == 0 ? q_out + ((size_t)h * M + m) * D
+                                  : (which == 1 ? k_cache : v_cache) + ((size_t)h * P + (P - M) + m) * D;
+  const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)m * H * D + (size_t)h * D);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int i = threadIdx.x; i < D / 8; i += blockDim.x) d4[i] = s[i];
+}
+
+}  // namespace kv
+}  // namespace fk
+
+extern "C" int fk_qkv_head_scatter(const void* q_src, const void* k_src, const void* v_src, void* q_out,
+                                   void* k_cache, void* v_cache, int M, int num_heads, int head_dim, int cache_len,
+                                   void* stream) {
+  FK_CHECK_ARG(q_src && k_src && v_src && q_out && k_cache && v_cache, "null tensor pointer");
+  FK_CHECK_ARG(M >= 1 && num_heads >= 1 && head_dim >= 8 && head_dim % 8 == 0, "bad sizes");
+  FK_CHECK_ARG(cache_len >= M, "cache_len must be >= M (new rows go to [cache_len - M, cache_len))");
+  kv::head_scatter_kernel<<<dim3(M, num_heads, 3), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q_src), static_cast<const __nv_bfloat16*>(k_src),
+      static_cast<const __nv_bfloat16*>(v_src), static_cast<__nv_bfloat16*>(q_out),
+      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), M, num_heads, head_dim,
+      cache_len);
+  FK_CHECK_CUDA(cudaGetLastError());
+  return kOk;
+}

@@ -198,3 +198,81 @@ def decode_attention(q, k_cache, v_cache, cache_seqlens, softmax_scale=None, num
     o_p, l_p = alloc_partials(B, Hq, S, dev)
     dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, softmax_scale)
     return out, lse
+
+
+class DAttn1:
+    """The reference's decode-attention kernel object, same constructor and call.
+
+    ``DAttn1(qk_mnk=(16, 128, 128), stages=2, p_stages=1, is_persistent=True)(Q, K, V, O, softmax_scale)``
+    computes ``O[h] = (Q[h] @ K[h]^T) @ V[h]`` with the scores rounded to bf16
+    and no softmax, exactly as python/cutedsl_kernels/decoding_attention/attn1.py:204-251
+    does (and as its check demo/dec_attn_second_part.py:33-34 expects). Q is
+    [H, M<=16, 128], K [H, P, 128], V is given transposed as [H, 128, P], O is
+    [H, M, 128]; all bf16. ``softmax_scale`` is accepted and, as in the
+    reference, not applied. The tuning arguments describe Hopper tiles and are
+    ignored. For softmax decode attention over a KV cache use
+    :class:`DecodeAttention`.
+    """
+
+    def __init__(self, qk_mnk=(16, 128, 128), stages: int = 2, p_stages: int = 1, is_persistent: bool = True):
+        self.qk_mnk = tuple(qk_mnk)
+
+    def __call__(self, Q, K, V, O, softmax_scale=1.0, stream=None):
+        require_tensor("Q", Q, torch.bfloat16, 3)
+        require_tensor("K", K, torch.bfloat16, 3)
+        require_tensor("V", V, torch.bfloat16, 3)
+        require_tensor("O", O, torch.bfloat16, 3)
+        H, M, D = Q.shape
+        P = K.shape[1]
+        require_shape("K", K, (H, P, D))
+        require_shape("V", V, (H, D, P))
+        require_shape("O", O, (H, M, D))
+        dev = same_device(Q, K, V, O)
+        st = stream_for(dev, stream)
+        _native.check(_native.load().fk_dattn1(ptr(Q), ptr(K), ptr(V), ptr(O), H, M, P, D, st))
+
+
+class DAttn2:
+    """The reference's fused QKV projection + KV-cache write, same constructor and call.
+
+    ``DAttn2(qkw_mnk, stg1_stages, persistent)(X, Wq, Wk, Wv, Q_out, K_cache, V_cache)``
+    (python/cutedsl_kernels/decoding_attention/attempt2.py:77-99): with X [M, H*D]
+    and W* [H*D, H*D] (row = output feature), writes ``Q_out[h] = (X Wq^T)[:, h]``
+    as [H, M, D] and the new K/V rows into ``K_cache/V_cache[h, P-M:P]`` of the
+    [H, P, D] caches, the layout of its check demo/dec_attn_run.py:51-63. Runs as
+    three weight-streaming GEMMs (x is M <= 16 tokens) and one head-major
+    scatter; the Hopper tuning arguments are ignored.
+    """
+
+    def __init__(self, qkw_mnk=(16, 128, 64), stg1_stages: int = 2, persistent: bool = False):
+        self.qkw_mnk = tuple(qkw_mnk)
+        self._tmp: dict = {}
+
+    def __call__(self, X, Wq, Wk, Wv, Q_out, K_cache, V_cache, stream=None):
+        from .gemm import linear
+
+        require_tensor("X", X, torch.bfloat16, 2)
+        require_tensor("Q_out", Q_out, torch.bfloat16, 3)
+        require_tensor("K_cache", K_cache, torch.bfloat16, 3)
+        require_tensor("V_cache", V_cache, torch.bfloat16, 3)
+        M, HD = X.shape
+        H, _, D = Q_out.shape
+        P = K_cache.shape[1]
+        require_shape("Q_out", Q_out, (H, M, D))
+        require_shape("K_cache", K_cache, (H, P, D))
+        require_shape("V_cache", V_cache, (H, P, D))
+        if H * D != HD:
+            raise ValueError(f"X has {HD} features but Q_out is [{H}, {M}, {D}]")
+        if P < M:
+            raise ValueError("cache length must be >= M")
+        dev = same_device(X, Wq, Wk, Wv, Q_out, K_cache, V_cache)
+        key = (M, HD, str(dev))
+        tmp = self._tmp.get(key)
+        if tmp is None:
+            tmp = torch.empty(3, M, HD, dtype=torch.bfloat16, device=dev)
+            self._tmp[key] = tmp
+        for i, w in enumerate((Wq, Wk, Wv)):
+            linear(X, w, tmp[i], stream=stream)
+        st = stream_for(dev, stream)
+        _native.check(_native.load().fk_qkv_head_scatter(
+            ptr(tmp[0]), ptr(tmp[1]), ptr(tmp[2]), ptr(Q_out), ptr(K_cache), ptr(V_cache), M, H, D, P, st))

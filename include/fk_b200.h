@@ -117,6 +117,25 @@ FK_API int fk_kv_append(const void* src, long long src_row_stride, int k_col, in
                         void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
                         int max_seqlen, int num_heads_kv, int head_dim, void* stream);
 
+/* Reference-semantics decode attention of DAttn1
+ * (python/cutedsl_kernels/decoding_attention/attn1.py:89-141, called as
+ * DAttn1(qk_mnk, stages, p_stages, is_persistent)(Q, K, V, O, softmax_scale)):
+ *   O[h] = bf16( bf16(Q[h] K[h]^T) V[h]^T ), no softmax, no scale
+ * Q [H, seq_q <= 16, 128], K [H, P, 128], v_t = V stored transposed [H, 128, P],
+ * O [H, seq_q, 128], all bf16; P % 8 == 0. */
+FK_API int fk_dattn1(const void* q, const void* k, const void* v_t, void* out, int num_heads, int seq_q,
+                     int seqlen_kv, int head_dim, void* stream);
+
+/* Head-major scatter of the three outputs of a QKV projection, the layout step
+ * of the reference's DAttn2 (python/cutedsl_kernels/decoding_attention/attempt2.py:270-286;
+ * check demo/dec_attn_run.py:51-63): with q/k/v_src [M, H*D],
+ *   q_out[h][m][d] = q_src[m][h*D + d],
+ *   k_cache[h][cache_len - M + m][d] = k_src[m][h*D + d] (and v likewise),
+ * q_out [H, M, D], caches [H, cache_len, D]; all bf16, 16-byte aligned. */
+FK_API int fk_qkv_head_scatter(const void* q_src, const void* k_src, const void* v_src, void* q_out,
+                               void* k_cache, void* v_cache, int M, int num_heads, int head_dim, int cache_len,
+                               void* stream);
+
 /* ---- linear family: y[M, N] = epilogue(x[M, K] . W[N, K]^T) ---------------
  * x bf16 [M, K] (K % 8 == 0, 16-byte aligned), W bf16 [N, K] (row = output
  * feature), y bf16 [M, N], fp32 accumulation. M <= 16 runs the persistent

@@ -175,3 +175,60 @@ def test_config2_ragged_full_size():
         assert_attn_close(out[r:r + 1], lse[r:r + 1], ro, rl)
     del k, v
     torch.cuda.empty_cache()
+
+
+def _normwise(out, ref):
+    out, ref = out.float().cpu(), ref.float().cpu()
+    return ((out - ref).abs().max() / ref.abs().max()).item()
+
+
+def test_dattn1_reference_semantics(golden):
+    """DAttn1's (Q K^T) V^T with bf16 scores: golden fixture from the reference's check, and the demo shape.
+
+    Scores reach ~|11| and sums over P tokens reach hundreds, so the bound is
+    normwise: max |out - ref| / max |ref| <= 1e-2 (bf16 scores and output).
+    """
+    from fused_kernels_cutedsl_lib_b200 import DAttn1, compile_cutedsl
+
+    g = golden("dattn1")
+    Q, K, V = g["Q"].cuda(), g["K"].cuda(), g["V"].cuda()
+    O = torch.empty_like(Q)
+    DAttn1(qk_mnk=(16, 128, 128), stages=2, p_stages=1, is_persistent=True)(Q, K, V, O, 1.0)
+    torch.cuda.synchronize()
+    assert _normwise(O, g["O"]) <= 1e-2
+    torch.manual_seed(42)  # the reference demo's shape: H=128 heads, M=16, P=1024
+    Q = torch.randn(128, 16, 128, device="cuda").bfloat16()
+    K = torch.randn(128, 1024, 128, device="cuda").bfloat16()
+    V = torch.randn(128, 128, 1024, device="cuda").bfloat16()
+    O = torch.empty(128, 16, 128, dtype=torch.bfloat16, device="cuda")
+    f = compile_cutedsl((Q, K, V, O, 1.0), DAttn1((16, 128, 128), 2, 1, True), False)
+    f(Q, K, V, O, 1.0)
+    torch.cuda.synchronize()
+    assert _normwise(O, oracle.dattn1_reference(Q, K, V)) <= 1e-2
+    # ragged P (multiple of 8, not of 16) and fewer query rows
+    Q2, K2, V2 = Q[:3, :5].contiguous(), K[:3, :200].contiguous(), V[:3, :, :200].contiguous()
+    O2 = torch.empty(3, 5, 128, dtype=torch.bfloat16, device="cuda")
+    DAttn1()(Q2, K2, V2, O2)
+    torch.cuda.synchronize()
+    assert _normwise(O2, oracle.dattn1_reference(Q2, K2, V2)) <= 1e-2
+
+
+def test_dattn2_qkv_projection_and_cache_write():
+    """DAttn2 against the layout of its reference check: X @ [WQ^T WK^T WV^T], chunk, view, transpose."""
+    from fused_kernels_cutedsl_lib_b200 import DAttn2
+
+    torch.manual_seed(42)
+    M, H, D, P = 16, 32, 128, 1024
+    X = torch.randn(M, H * D, device="cuda").bfloat16()
+    Ws = [(torch.randn(H * D, H * D, device="cuda") * 0.02).bfloat16() for _ in range(3)]
+    Q_out = torch.zeros(H, M, D, dtype=torch.bfloat16, device="cuda")
+    Kc = torch.zeros(H, P, D, dtype=torch.bfloat16, device="cuda")
+    Vc = torch.zeros(H, P, D, dtype=torch.bfloat16, device="cuda")
+    DAttn2((16, 128, 64), 2, False)(X, *Ws, Q_out, Kc, Vc)
+    torch.cuda.synchronize()
+    qkv = torch.cat([oracle.linear(X, w) for w in Ws], dim=1)  # [M, 3*H*D]
+    q, k, v = (t.view(M, H, D).transpose(0, 1) for t in qkv.chunk(3, dim=-1))
+    for got, ref in ((Q_out, q), (Kc[:, P - M:], k), (Vc[:, P - M:], v)):
+        e = (got.float().cpu() - ref).abs() / ref.abs().clamp_min(1.0)
+        assert e.max().item() <= 2e-2 and e.mean().item() <= 2e-3
+    assert torch.all(Kc[:, :P - M] == 0) and torch.all(Vc[:, :P - M] == 0)
