@@ -99,12 +99,51 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB_PATH
 
 
+TVMFFI_SRC = PKG_DIR / "tvmffi" / "fk_tvmffi.cc"
+TVMFFI_LIB = LIB_DIR / "libfk_b200_tvmffi.so"
+
+
+def tvm_ffi_paths():
+    """(include dirs, lib dir) of the installed apache-tvm-ffi, or None if absent."""
+    import importlib.util
+
+    spec = importlib.util.find_spec("tvm_ffi")
+    if spec is None or not spec.submodule_search_locations:
+        return None
+    root = Path(list(spec.submodule_search_locations)[0])
+    inc, lib = root / "include", root / "lib"
+    if not (inc / "tvm" / "ffi" / "function.h").exists() or not (lib / "libtvm_ffi.so").exists():
+        return None
+    dl = root / "3rdparty" / "dlpack" / "include"
+    incs = [inc] + ([dl] if dl.exists() else [])
+    return incs, lib
+
+
+def build_tvmffi(force: bool = False) -> Path | None:
+    """TVM-FFI module over libfk_b200 (skipped when apache-tvm-ffi is not installed)."""
+    paths = tvm_ffi_paths()
+    if paths is None:
+        return None
+    incs, libdir = paths
+    if not force and not _stale(TVMFFI_LIB, [TVMFFI_SRC, LIB_PATH, INCLUDE_DIR / "fk_b200.h"]):
+        return TVMFFI_LIB
+    cxx = shutil.which("g++") or "c++"
+    cmd = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", str(TVMFFI_SRC), "-o", str(TVMFFI_LIB),
+           f"-I{INCLUDE_DIR}", *[f"-I{i}" for i in incs], f"-L{LIB_DIR}", "-lfk_b200", f"-L{libdir}", "-ltvm_ffi",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{libdir}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"TVM-FFI module build failed:\n{res.stdout}\n{res.stderr}")
+    return TVMFFI_LIB
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true", help="print ptxas register usage")
     args = ap.parse_args()
     print(build(force=args.force, verbose=args.verbose))
+    print(build_tvmffi(force=args.force))
 
 
 if __name__ == "__main__":

@@ -1,0 +1,126 @@
+// TVM-FFI entry points over the C ABI of libfk_b200 (include/fk_b200.h).
+//
+// The reference requires its kernels to be TVM-FFI functions taking torch
+// tensors (README.md:1; compiled with `--enable-tvm-ffi`,
+// python/cdsl_helpers/cdsl_fn_utils.py:38-44). This module provides that
+// surface for the sm_100a kernels: every function takes DLPack tensor views
+// (torch tensors pass straight through tvm_ffi), launches on the environment
+// stream of the tensors' device (TVMFFIEnvGetStream, the current torch stream
+// when called from torch) and raises ValueError / RuntimeError with the
+// library's message on a bad status. Outputs and scratch are caller-allocated.
+#include <tvm/ffi/container/tensor.h>
+#include <tvm/ffi/error.h>
+#include <tvm/ffi/extra/c_env_api.h>
+#include <tvm/ffi/function.h>
+
+#include <cmath>
+#include <string>
+
+#include "fk_b200.h"
+
+namespace {
+
+using tvm::ffi::TensorView;
+
+void* stream_of(const TensorView& t) {
+  return TVMFFIEnvGetStream(t.device().device_type, t.device().device_id);
+}
+
+void check(int rc) {
+  if (rc == 0) return;
+  const std::string msg = fk_last_error();
+  if (rc == -1) TVM_FFI_THROW(ValueError) << msg;
+  TVM_FFI_THROW(RuntimeError) << "libfk_b200 status " << rc << ": " << msg;
+}
+
+void use(const TensorView& t) { check(fk_use_device(t.device().device_id)); }
+
+size_t nbytes(const TensorView& t) {
+  size_t n = (t.dtype().bits + 7) / 8;
+  for (int i = 0; i < t.ndim(); ++i) n *= static_cast<size_t>(t.size(i));
+  return n;
+}
+
+void require(bool ok, const char* msg) {
+  if (!ok) TVM_FFI_THROW(ValueError) << msg;
+}
+
+// ---- split-KV decode attention -------------------------------------------
+void dec_attn_splitkv_fwd(TensorView q, TensorView k_cache, TensorView v_cache, TensorView cache_seqlens,
+                          TensorView out, TensorView lse, TensorView o_partial, TensorView lse_partial,
+                          int64_t num_splits, double softmax_scale) {
+  require(k_cache.ndim() == 4, "k_cache must be [B, Lmax, Hkv, D]");
+  use(q);
+  const int B = (int)k_cache.size(0), L = (int)k_cache.size(1), Hkv = (int)k_cache.size(2);
+  const int D = (int)k_cache.size(3);
+  const int Hq = (int)(q.ndim() == 4 ? q.size(2) : q.size(1));
+  const float scale = softmax_scale > 0 ? (float)softmax_scale : 1.0f / std::sqrt((float)D);
+  check(fk_dec_attn_fwd(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                        static_cast<const int32_t*>(cache_seqlens.data_ptr()), out.data_ptr(),
+                        static_cast<float*>(lse.data_ptr()), static_cast<float*>(o_partial.data_ptr()),
+                        static_cast<float*>(lse_partial.data_ptr()), B, L, Hq, Hkv, D, (int)num_splits, scale,
+                        stream_of(q)));
+}
+
+void dec_attn_combine(TensorView o_partial, TensorView lse_partial, TensorView cache_seqlens, TensorView out,
+                      TensorView lse, int64_t max_seqlen) {
+  require(o_partial.ndim() == 4, "o_partial must be [S, B, Hq, D]");
+  use(o_partial);
+  check(fk_dec_attn_combine(static_cast<const float*>(o_partial.data_ptr()),
+                            static_cast<const float*>(lse_partial.data_ptr()),
+                            static_cast<const int32_t*>(cache_seqlens.data_ptr()), out.data_ptr(),
+                            static_cast<float*>(lse.data_ptr()), (int)o_partial.size(1), (int)max_seqlen,
+                            (int)o_partial.size(2), (int)o_partial.size(3), (int)o_partial.size(0),
+                            stream_of(o_partial)));
+}
+
+void dattn1(TensorView Q, TensorView K, TensorView V, TensorView O, double softmax_scale) {
+  (void)softmax_scale;  // unused, as in the reference kernel
+  use(Q);
+  check(fk_dattn1(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), (int)Q.size(0), (int)Q.size(1),
+                  (int)K.size(1), (int)Q.size(2), stream_of(Q)));
+}
+
+// ---- linear family (x [M, K], w [N, K], y [M, N]; workspace zero-filled) ---
+void skinny_gemm(TensorView x, TensorView w, TensorView y, TensorView workspace) {
+  use(x);
+  check(fk_skinny_gemm(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)w.size(0), (int)x.size(1),
+                       workspace.data_ptr(), nbytes(workspace), stream_of(x)));
+}
+
+void rmsnorm_linear(TensorView x, TensorView gamma, TensorView w, TensorView y, double eps, TensorView workspace) {
+  use(x);
+  check(fk_rmsnorm_linear(x.data_ptr(), gamma.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0),
+                          (int)w.size(0), (int)x.size(1), (float)eps, workspace.data_ptr(), nbytes(workspace),
+                          stream_of(x)));
+}
+
+void swiglu_gemm(TensorView x, TensorView w_gate_up, TensorView y, TensorView workspace) {
+  use(x);
+  check(fk_swiglu_gemm(x.data_ptr(), w_gate_up.data_ptr(), y.data_ptr(), (int)x.size(0),
+                       (int)(w_gate_up.size(0) / 2), (int)x.size(1), workspace.data_ptr(), nbytes(workspace),
+                       stream_of(x)));
+}
+
+void swiglu_gemm2(TensorView x, TensorView b, TensorView b1, TensorView y, TensorView workspace) {
+  use(x);
+  check(fk_swiglu_gemm2(x.data_ptr(), b.data_ptr(), b1.data_ptr(), y.data_ptr(), (int)x.size(0), (int)b.size(0),
+                        (int)x.size(1), workspace.data_ptr(), nbytes(workspace), stream_of(x)));
+}
+
+int64_t linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t swiglu) {
+  size_t b = 0;
+  check(fk_linear_workspace_bytes((int)M, (int)N, (int)K, swiglu ? FK_LINEAR_SWIGLU : 0, &b));
+  return (int64_t)b;
+}
+
+}  // namespace
+
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_splitkv_fwd, dec_attn_splitkv_fwd);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_combine, dec_attn_combine);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(dattn1, dattn1);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(skinny_gemm, skinny_gemm);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(rmsnorm_linear, rmsnorm_linear);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm, swiglu_gemm);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm2, swiglu_gemm2);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(linear_workspace_bytes, linear_workspace_bytes);

@@ -61,3 +61,13 @@ def test_python_entry_points_reject_bad_tensors():
         decode_attention(q.float(), k, k, torch.zeros(2, dtype=torch.int32))
     with pytest.raises(ValueError):  # CPU tensors
         decode_attention(q, k, k, torch.zeros(2, dtype=torch.int32))
+
+
+def test_tvm_ffi_module_loads_and_exports():
+    pytest.importorskip("tvm_ffi")
+    from fused_kernels_cutedsl_lib_b200 import tvm_ffi_module
+
+    mod = tvm_ffi_module.load()
+    for name in ("dec_attn_splitkv_fwd", "dec_attn_combine", "dattn1", "skinny_gemm", "rmsnorm_linear",
+                 "swiglu_gemm", "swiglu_gemm2", "linear_workspace_bytes"):
+        assert getattr(mod, name) is not None

@@ -203,3 +203,26 @@ def test_shared_workspace_across_shapes():
             skinny_gemm(x, w, y, workspace=ws)
             finish()
             assert_close(y, oracle.linear(x, w))
+
+
+def test_tvm_ffi_entry_points_match_ctypes():
+    """The TVM-FFI module (torch tensors in, reference style) gives the same results as the ctypes path."""
+    pytest.importorskip("tvm_ffi")
+    from fused_kernels_cutedsl_lib_b200 import tvm_ffi_module
+
+    mod = tvm_ffi_module.load()
+    x, w = mk(16, 4096, 4096, seed=8)
+    gam = gamma_of(4096)
+    ws = alloc_workspace(int(mod.linear_workspace_bytes(16, 4096, 4096, 1)), "cuda")
+    y = torch.empty(16, 4096, dtype=torch.bfloat16, device="cuda")
+    mod.skinny_gemm(x, w, y, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(y, skinny_gemm(x, w))
+    mod.rmsnorm_linear(x, gam, w, y, 1e-6, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(y, rmsnorm_linear(x, gam, w, eps=1e-6))
+    wgu = mk(16, 2 * 2048, 4096, seed=9)[1]
+    y2 = torch.empty(16, 2048, dtype=torch.bfloat16, device="cuda")
+    mod.swiglu_gemm(x, wgu, y2, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(y2, swiglu_gemm(x, wgu))
