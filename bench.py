@@ -404,20 +404,18 @@ def run_layer(args):
         y_h.copy_(layer(x_d, k, v, lens), non_blocking=True)
 
     step_e2e = e2e_body
-    # Graph capture is used on one GPU only: a capture of the tensor-parallel step
-    # (NCCL all-gathers interleaved with programmatic-dependent launches) did not
-    # complete on the GPU box, so N > 1 launches eagerly until that is resolved.
-    use_graph = not args.no_graph and world == 1
+    use_graph = not args.no_graph
+    graphs = []
     if use_graph:
         # One decode step (7 launches on 1 GPU; + 5 all-gathers under TP) captured
         # once and replayed: no per-launch host work inside the timed loop.
-        g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g1):
+        graphs = [torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()]
+        with torch.cuda.graph(graphs[0]):
             layer(x, k, v, lens)
-        with torch.cuda.graph(g2):
+        with torch.cuda.graph(graphs[1]):
             e2e_body()
         torch.cuda.synchronize()
-        step, step_e2e = g1.replay, g2.replay
+        step, step_e2e = graphs[0].replay, graphs[1].replay
         for _ in range(2):
             step()
         torch.cuda.synchronize()
@@ -459,7 +457,7 @@ def run_layer(args):
             "config": {"workload": "decode_layer_config5", "batch": B, "context": ctx, "hidden": H, "ffn": F,
                        "heads_q": HQ, "heads_kv": HKV,
                        "parallelism": "single GPU" if world == 1 else f"tp{world} GEMMs + batch-sharded attention",
-                       "cuda_graph": (not args.no_graph) and world == 1,
+                       "cuda_graph": not args.no_graph,
                        "l2": "weights 436 MB + KV 4.3 GB per step exceed L2"},
             "bytes_per_step": wbytes + kv_bytes,
             "achieved_TBps": round((wbytes + kv_bytes) / world / (ms * 1e-3) / 1e12, 3),
@@ -469,6 +467,11 @@ def run_layer(args):
             "gpu_launches": args.steps * (7 if world == 1 else 7),
             "clocks": clk,
         }), flush=True)
+    # Graphs that captured NCCL collectives must be freed before the process
+    # group is destroyed (destroying it first hangs at exit).
+    step = step_e2e = None
+    graphs.clear()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
