@@ -59,6 +59,15 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "fk_dattn1": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
     "fk_qkv_head_scatter": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
+    "fk_dec_attn_fwd_paged": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_float, _p],
+    ),
+    "fk_kv_append_paged": (
+        _c_int,
+        [_p, ctypes.c_longlong, _c_int, _c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _p],
+    ),
     "fk_rmsnorm_swiglu": (
         _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
 }

@@ -41,6 +41,8 @@ constexpr int STAGE_BYTES = 2 * TILE_BYTES;// K + V: 32 KB
 struct Params {
   const __nv_bfloat16* q;  // row b at q + b * q_stride: [Hq, D] contiguous
   long long q_stride;      // elements between batch rows of q (Hq * D when dense)
+  const int* block_table;  // paged cache: [B, max_blocks] physical block of each logical block (or null)
+  int max_blocks, block_size;
   const int* seqlens;      // [B]
   float* o_part;           // [S, B, Hq, D]
   float* lse_part;         // [S, B, Hq]
@@ -135,10 +137,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t* kd = ring + stage * STAGE_BYTES;
           uint8_t* vd = kd + TILE_BYTES;
-          tma_load_4d(kd, &tmK, &full[stage], 0, h, t, b, pol);
-          tma_load_4d(kd + HALF_BYTES, &tmK, &full[stage], 64, h, t, b, pol);
-          tma_load_4d(vd, &tmV, &full[stage], 0, h, t, b, pol);
-          tma_load_4d(vd + HALF_BYTES, &tmV, &full[stage], 64, h, t, b, pol);
+          // Contiguous cache: (token, row). Paged: (token within block, physical
+          // block); a 64-token tile never crosses a block (block_size % 64 == 0).
+          int ct = t, cb = b;
+          if (p.block_table) {
+            cb = __ldg(p.block_table + (size_t)b * p.max_blocks + t / p.block_size);
+            ct = t % p.block_size;
+          }
+          tma_load_4d(kd, &tmK, &full[stage], 0, h, ct, cb, pol);
+          tma_load_4d(kd + HALF_BYTES, &tmK, &full[stage], 64, h, ct, cb, pol);
+          tma_load_4d(vd, &tmV, &full[stage], 0, h, ct, cb, pol);
+          tma_load_4d(vd + HALF_BYTES, &tmV, &full[stage], 64, h, ct, cb, pol);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -428,10 +437,13 @@ int fk_dec_attn_chunk_tokens(int max_seqlen, int num_splits) {
   return attn::chunk_tokens(max_seqlen, num_splits);
 }
 
+// Paged form when block_table != null: k_cache/v_cache are block pools
+// [num_blocks, block_size, Hkv, D] and max_seqlen = max_blocks * block_size.
 static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cache, const void* v_cache,
                             const int32_t* cache_seqlens, float* o_partial, float* lse_partial,
                             int batch, int max_seqlen, int num_heads_q, int num_heads_kv,
-                            int head_dim, int num_splits, float softmax_scale, void* stream) {
+                            int head_dim, int num_splits, float softmax_scale, void* stream,
+                            const int32_t* block_table = nullptr, int block_size = 0, int num_blocks = 0) {
   FK_CHECK_ARG(q_stride >= (long long)num_heads_q * head_dim && q_stride % 8 == 0,
                "q row stride must be >= num_heads_q * head_dim and a multiple of 8");
   int rc = check_attn_args(q, k_cache, v_cache, cache_seqlens, batch, max_seqlen, num_heads_q,
@@ -445,6 +457,9 @@ static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cac
   attn::Params p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_stride = q_stride;
+  p.block_table = block_table;
+  p.block_size = block_table ? block_size : 0;
+  p.max_blocks = block_table ? max_seqlen / block_size : 0;
   p.seqlens = cache_seqlens;
   p.o_part = o_partial;
   p.lse_part = lse_partial;
@@ -459,10 +474,11 @@ static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cac
 
   // K/V cache [B, Lmax, Hkv, 128] bf16 viewed as a 4-D tensor (dim, head, token, batch).
   CUtensorMap tmK, tmV;
-  const uint64_t dims[4] = {(uint64_t)attn::D, (uint64_t)num_heads_kv, (uint64_t)max_seqlen,
-                            (uint64_t)batch};
+  const uint64_t rows = block_table ? (uint64_t)block_size : (uint64_t)max_seqlen;
+  const uint64_t outer = block_table ? (uint64_t)num_blocks : (uint64_t)batch;
+  const uint64_t dims[4] = {(uint64_t)attn::D, (uint64_t)num_heads_kv, rows, outer};
   const uint64_t strides[3] = {(uint64_t)attn::D * 2, (uint64_t)num_heads_kv * attn::D * 2,
-                               (uint64_t)max_seqlen * num_heads_kv * attn::D * 2};
+                               rows * num_heads_kv * attn::D * 2};
   const uint32_t box[4] = {64, 1, (uint32_t)attn::T, 1};
   rc = encode_tma(&tmK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k_cache), dims,
                   strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -492,6 +508,24 @@ int fk_dec_attn_fwd_ex(const void* q, long long q_batch_stride, const void* k_ca
                             max_seqlen, num_heads_q, num_heads_kv, head_dim, num_splits, softmax_scale, stream);
   if (rc) return rc;
   return fk_dec_attn_combine(o_partial, lse_partial, cache_seqlens, out, lse, batch, max_seqlen, num_heads_q,
+                             head_dim, num_splits, stream);
+}
+
+int fk_dec_attn_fwd_paged(const void* q, const void* k_pool, const void* v_pool, const int32_t* block_table,
+                          const int32_t* cache_seqlens, void* out, float* lse, float* o_partial,
+                          float* lse_partial, int batch, int max_blocks_per_seq, int block_size, int num_blocks,
+                          int num_heads_q, int num_heads_kv, int head_dim, int num_splits, float softmax_scale,
+                          void* stream) {
+  FK_CHECK_ARG(block_table != nullptr, "block_table is null");
+  FK_CHECK_ARG(block_size >= 64 && block_size % 64 == 0, "block_size must be a positive multiple of 64");
+  FK_CHECK_ARG(max_blocks_per_seq >= 1 && num_blocks >= 1, "max_blocks_per_seq and num_blocks must be >= 1");
+  const long long Lmax = (long long)max_blocks_per_seq * block_size;
+  FK_CHECK_ARG(Lmax < (1LL << 31), "max_blocks_per_seq * block_size too large");
+  int rc = splitkv_fwd_impl(q, (long long)num_heads_q * head_dim, k_pool, v_pool, cache_seqlens, o_partial,
+                            lse_partial, batch, (int)Lmax, num_heads_q, num_heads_kv, head_dim, num_splits,
+                            softmax_scale, stream, block_table, block_size, num_blocks);
+  if (rc) return rc;
+  return fk_dec_attn_combine(o_partial, lse_partial, cache_seqlens, out, lse, batch, (int)Lmax, num_heads_q,
                              head_dim, num_splits, stream);
 }
 

@@ -35,10 +35,53 @@ __global__ void __launch_bounds__(128) append_kernel(const __nv_bfloat16* __rest
   if (threadIdx.x == 0 && seqlens_out) seqlens_out[b] = ok ? pos + 1 : pos;
 }
 
+// Paged form: the row of token pos lives in block block_table[b][pos / bs], row pos % bs.
+__global__ void __launch_bounds__(128) append_paged_kernel(const __nv_bfloat16* __restrict__ src,
+                                                           long long src_stride, int k_col, int v_col,
+                                                           __nv_bfloat16* __restrict__ kp, __nv_bfloat16* __restrict__ vp,
+                                                           const int* __restrict__ block_table, int max_blocks, int bs,
+                                                           const int* seqlens_in, int* seqlens_out, int row_elems) {
+  const int b = blockIdx.x;
+  const int pos = seqlens_in[b];
+  __syncthreads();
+  const bool ok = pos >= 0 && pos < max_blocks * bs;
+  if (ok) {
+    const int blk = block_table[(size_t)b * max_blocks + pos / bs];
+    const size_t row = (size_t)blk * bs + pos % bs;
+    const uint4* ks = reinterpret_cast<const uint4*>(src + (size_t)b * src_stride + k_col);
+    const uint4* vs = reinterpret_cast<const uint4*>(src + (size_t)b * src_stride + v_col);
+    uint4* kd = reinterpret_cast<uint4*>(kp + row * row_elems);
+    uint4* vd = reinterpret_cast<uint4*>(vp + row * row_elems);
+    for (int i = threadIdx.x; i < row_elems / 8; i += blockDim.x) {
+      kd[i] = ks[i];
+      vd[i] = vs[i];
+    }
+  }
+  if (threadIdx.x == 0 && seqlens_out) seqlens_out[b] = ok ? pos + 1 : pos;
+}
+
 }  // namespace kv
 }  // namespace fk
 
 using namespace fk;
+
+extern "C" int fk_kv_append_paged(const void* src, long long src_row_stride, int k_col, int v_col, void* k_pool,
+                                  void* v_pool, const int32_t* block_table, const int32_t* cache_seqlens,
+                                  int32_t* seqlens_out, int batch, int max_blocks_per_seq, int block_size,
+                                  int num_heads_kv, int head_dim, void* stream) {
+  FK_CHECK_ARG(src && k_pool && v_pool && block_table && cache_seqlens, "null tensor pointer");
+  FK_CHECK_ARG(batch >= 1 && max_blocks_per_seq >= 1 && block_size >= 1 && num_heads_kv >= 1 && head_dim >= 8,
+               "sizes must be positive");
+  const int row = num_heads_kv * head_dim;
+  FK_CHECK_ARG(row % 8 == 0 && src_row_stride % 8 == 0 && k_col % 8 == 0 && v_col % 8 == 0,
+               "row length, stride and column offsets must be multiples of 8 elements");
+  kv::append_paged_kernel<<<batch, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), src_row_stride, k_col, v_col, static_cast<__nv_bfloat16*>(k_pool),
+      static_cast<__nv_bfloat16*>(v_pool), block_table, max_blocks_per_seq, block_size, cache_seqlens, seqlens_out,
+      row);
+  FK_CHECK_CUDA(cudaGetLastError());
+  return kOk;
+}
 
 extern "C" int fk_kv_append(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
                             void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,

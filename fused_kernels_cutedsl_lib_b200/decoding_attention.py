@@ -276,3 +276,36 @@ class DAttn2:
         st = stream_for(dev, stream)
         _native.check(_native.load().fk_qkv_head_scatter(
             ptr(tmp[0]), ptr(tmp[1]), ptr(tmp[2]), ptr(Q_out), ptr(K_cache), ptr(V_cache), M, H, D, P, st))
+
+
+def dec_attn_paged_fwd(q, k_pool, v_pool, block_table, cache_seqlens, out, lse, o_partial, lse_partial,
+                       num_splits: int, softmax_scale: float | None = None, stream=None) -> None:
+    """Split-KV decode attention over a paged KV cache (both passes).
+
+    ``k_pool``/``v_pool``: [num_blocks, block_size, Hkv, 128] bf16 with
+    ``block_size % 64 == 0``; ``block_table``: [B, max_blocks] int32, logical
+    block j of row b at physical block ``block_table[b, j]``. Splits follow
+    ``max_seqlen = max_blocks * block_size`` (``chunk_tokens``). Same outputs
+    as :func:`dec_attn_splitkv_fwd` on the equivalent contiguous cache.
+    """
+    require_tensor("q", q, torch.bfloat16)
+    require_tensor("k_pool", k_pool, torch.bfloat16, 4)
+    require_tensor("v_pool", v_pool, torch.bfloat16, 4)
+    require_tensor("block_table", block_table, torch.int32, 2)
+    require_tensor("cache_seqlens", cache_seqlens, torch.int32, 1)
+    NB, BS, Hkv, D = k_pool.shape
+    require_shape("v_pool", v_pool, (NB, BS, Hkv, D))
+    B, MB = block_table.shape
+    Hq = q.shape[-2]
+    if q.numel() != B * Hq * D or D != HEAD_DIM:
+        raise ValueError(f"q must be [B, 1, Hq, {HEAD_DIM}] with B={B}")
+    require_shape("cache_seqlens", cache_seqlens, (B,))
+    _check_partials(o_partial, lse_partial, num_splits, B, Hq)
+    require_tensor("out", out, torch.bfloat16)
+    require_tensor("lse", lse, torch.float32, 2)
+    dev = same_device(q, k_pool, v_pool, block_table, cache_seqlens, out, lse, o_partial, lse_partial)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    st = stream_for(dev, stream)
+    _native.check(_native.load().fk_dec_attn_fwd_paged(
+        ptr(q), ptr(k_pool), ptr(v_pool), ptr(block_table), ptr(cache_seqlens), ptr(out), ptr(lse),
+        ptr(o_partial), ptr(lse_partial), B, MB, BS, NB, Hq, Hkv, D, num_splits, scale, st))

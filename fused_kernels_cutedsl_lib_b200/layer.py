@@ -78,6 +78,19 @@ def kv_append(qkv, k_cache, v_cache, cache_seqlens, num_heads_q, num_heads_kv, s
         ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), B, L, num_heads_kv, HEAD_DIM, st))
 
 
+def kv_append_paged(qkv, k_pool, v_pool, block_table, cache_seqlens, num_heads_q, num_heads_kv, seqlens_out=None,
+                    stream=None):
+    """Paged form of :func:`kv_append`: row len of b goes to block ``block_table[b, len // bs]``."""
+    B, MB = block_table.shape
+    bs = k_pool.shape[1]
+    st = stream_for(qkv.device, stream)
+    out = cache_seqlens if seqlens_out is None else seqlens_out
+    _native.check(_native.load().fk_kv_append_paged(
+        ptr(qkv), qkv.stride(0), num_heads_q * HEAD_DIM, (num_heads_q + num_heads_kv) * HEAD_DIM,
+        ptr(k_pool), ptr(v_pool), ptr(block_table), ptr(cache_seqlens), ptr(out), B, MB, bs, num_heads_kv,
+        HEAD_DIM, st))
+
+
 def attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_partial, lse_partial, num_splits,
                        num_heads_q, num_heads_kv, softmax_scale=None, stream=None):
     """Split-KV attention reading q from the first ``Hq*128`` columns of each ``qkv`` row."""

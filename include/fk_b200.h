@@ -106,6 +106,25 @@ FK_API int fk_dec_attn_fwd_ex(const void* q, long long q_batch_stride, const voi
                               int num_heads_q, int num_heads_kv, int head_dim, int num_splits,
                               float softmax_scale, void* stream);
 
+/* Paged KV cache: k_pool / v_pool [num_blocks, block_size, Hkv, 128] bf16 and
+ * block_table [batch, max_blocks_per_seq] int32 (logical block j of row b is
+ * physical block block_table[b][j]); block_size must be a multiple of 64 and
+ * splits follow max_seqlen = max_blocks_per_seq * block_size. Entries past a
+ * row's length are never read. Otherwise as fk_dec_attn_fwd. (The reference
+ * has only a contiguous cache, decoding_attention/attn1.py:92-94.) */
+FK_API int fk_dec_attn_fwd_paged(const void* q, const void* k_pool, const void* v_pool,
+                                 const int32_t* block_table, const int32_t* cache_seqlens, void* out, float* lse,
+                                 float* o_partial, float* lse_partial, int batch, int max_blocks_per_seq,
+                                 int block_size, int num_blocks, int num_heads_q, int num_heads_kv, int head_dim,
+                                 int num_splits, float softmax_scale, void* stream);
+
+/* Paged form of fk_kv_append: the new row of b goes to block
+ * block_table[b][len / block_size], row len % block_size (any block_size >= 1). */
+FK_API int fk_kv_append_paged(const void* src, long long src_row_stride, int k_col, int v_col, void* k_pool,
+                              void* v_pool, const int32_t* block_table, const int32_t* cache_seqlens,
+                              int32_t* seqlens_out, int batch, int max_blocks_per_seq, int block_size,
+                              int num_heads_kv, int head_dim, void* stream);
+
 /* KV-cache append: for each row b with 0 <= cache_seqlens[b] < max_seqlen,
  * copy the new K row (src + b*src_row_stride + k_col, num_heads_kv*head_dim
  * bf16) and V row (… + v_col) into k_cache/v_cache[b, cache_seqlens[b]] and

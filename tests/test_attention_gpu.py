@@ -232,3 +232,52 @@ def test_dattn2_qkv_projection_and_cache_write():
         e = (got.float().cpu() - ref).abs() / ref.abs().clamp_min(1.0)
         assert e.max().item() <= 2e-2 and e.mean().item() <= 2e-3
     assert torch.all(Kc[:, :P - M] == 0) and torch.all(Vc[:, :P - M] == 0)
+
+
+@pytest.mark.parametrize("block_size", [64, 256])
+def test_paged_kv_cache_matches_contiguous(block_size):
+    """Paged attention over a shuffled block pool equals contiguous attention on the gathered cache."""
+    from fused_kernels_cutedsl_lib_b200.decoding_attention import dec_attn_paged_fwd
+    from fused_kernels_cutedsl_lib_b200.layer import kv_append_paged
+
+    torch.manual_seed(21)
+    B, Hq, Hkv, MB = 6, 32, 8, 12
+    L = MB * block_size
+    lens = torch.tensor([L, 1, 0, 65, L - 7, 300], dtype=torch.int32)
+    NB = B * MB + 5
+    perm = torch.randperm(NB)[: B * MB].view(B, MB).to(torch.int32)
+    k_pool = torch.randn(NB, block_size, Hkv, 128, device="cuda").bfloat16()
+    v_pool = torch.randn(NB, block_size, Hkv, 128, device="cuda").bfloat16()
+    q = torch.randn(B, 1, Hq, 128, device="cuda").bfloat16()
+    table = perm.cuda()
+    flat = perm.long().view(-1)
+    k = k_pool[flat].view(B, MB * block_size, Hkv, 128).contiguous()
+    v = v_pool[flat].view(B, MB * block_size, Hkv, 128).contiguous()
+    S = 5
+    outs = []
+    for paged in (False, True):
+        out = torch.full((B, 1, Hq, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+        lse = torch.empty(B, Hq, device="cuda")
+        o_p, l_p = alloc_partials(B, Hq, S, "cuda")
+        if paged:
+            dec_attn_paged_fwd(q, k_pool, v_pool, table, lens.cuda(), out, lse, o_p, l_p, S)
+        else:
+            dec_attn_splitkv_fwd(q, k, v, lens.cuda(), out, lse, o_p, l_p, S)
+        torch.cuda.synchronize()
+        outs.append((out, lse))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    ref_out, ref_lse = oracle.decode_attention(q, k, v, lens)
+    assert_attn_close(outs[1][0], outs[1][1], ref_out, ref_lse)
+    # paged append: the new rows land at (block_table[b][len // bs], len % bs)
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * 128, device="cuda").bfloat16()
+    lens_d = torch.tensor([5, 0, 64, block_size, 17, L - 1], dtype=torch.int32, device="cuda")
+    before = lens_d.clone().cpu()
+    kv_append_paged(qkv, k_pool, v_pool, table, lens_d, Hq, Hkv)
+    torch.cuda.synchronize()
+    for b in range(B):
+        pos = int(before[b])
+        blk = int(perm[b, pos // block_size])
+        got = k_pool[blk, pos % block_size].reshape(-1)
+        assert torch.equal(got, qkv[b, Hq * 128:(Hq + Hkv) * 128])
+        assert torch.equal(v_pool[blk, pos % block_size].reshape(-1), qkv[b, (Hq + Hkv) * 128:])
+    assert lens_d.cpu().tolist() == (before + 1).tolist()
