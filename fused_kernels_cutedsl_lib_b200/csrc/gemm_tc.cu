@@ -40,7 +40,7 @@ namespace tc {
 
 constexpr int BM = 128;         // W rows per row block (UMMA M)
 constexpr int BK = 64;          // k per stage: one 128B swizzle atom of bf16
-constexpr int NTHREADS = 192;   // 6 warps
+constexpr int NTHREADS = 224;   // 7 warps
 constexpr int EPI_WARP0 = 2;
 constexpr int EPI_THREADS = 128;
 constexpr int WBOX = BM * 128;  // 16 KB
@@ -48,20 +48,28 @@ constexpr int NORM_TILE = 128;  // tokens per launch with RMSNorm (hi + lo = 256
 constexpr size_t kSmemBudget = 227 * 1024;
 constexpr int kMaxGrid = 192;   // persistent grid bound (148 SMs on B200)
 
+// Two TMA rings: a deep one for the weight tiles (streamed from HBM, long
+// latency) and a shallower one for the x tiles (re-read from L2 every k block,
+// short latency), so that large token tiles do not crowd weights out of the
+// bytes in flight.
 template <int NMMA, bool SWIGLU>
 struct Layout {
   static constexpr int W_BYTES = WBOX * (SWIGLU ? 2 : 1);
-  static constexpr int X_OFF = W_BYTES;
   static constexpr int X_BYTES = NMMA * 128;
-  static constexpr int TX = W_BYTES + X_BYTES;
-  static constexpr int STAGE_BYTES = (X_OFF + X_BYTES + 1023) / 1024 * 1024;
-  static constexpr int STAGES_FIT = (int)((kSmemBudget - 4096) / (STAGE_BYTES + 16));
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SX = (X_BYTES >= 32768 && SWIGLU) ? 2 : (X_BYTES >= 16384 ? 3 : 4);
+  static constexpr int SW_FIT = (int)((kSmemBudget - 4096 - (size_t)SX * X_BYTES) / (W_BYTES + 16));
+  static constexpr int SW = SW_FIT > 8 ? 8 : SW_FIT;
+  static constexpr int STAGES = SW;
+  static constexpr int X_RING = SW * W_BYTES;
   static constexpr int ACC_COLS = NMMA * (SWIGLU ? 2 : 1);
-  static constexpr int TMEM_COLS = ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
-                                   : ACC_COLS <= 256 ? 256 : 512;
-  // barriers: full + empty per stage, acc_full, acc_empty, done; TMEM address
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (2 * STAGES + 3) * 8 + 16;
+  // Two accumulator buffers when they fit in TMEM's 512 columns: the MMA warp
+  // fills one while the epilogue drains the other.
+  static constexpr int NBUF = 2 * ACC_COLS <= 512 ? 2 : 1;
+  static constexpr int TMEM_NEED = NBUF * ACC_COLS;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                   : TMEM_NEED <= 256 ? 256 : 512;
+  // barriers: full + empty per W and x stage, acc_full[2], acc_empty[2], done; TMEM address
+  static constexpr size_t SMEM = 1024 + (size_t)SW * W_BYTES + (size_t)SX * X_BYTES + (2 * SW + 2 * SX + 5) * 8 + 16;
 };
 
 __host__ __device__ constexpr int slot_floats(int nmma, bool swiglu) { return nmma * BM * (swiglu ? 2 : 1); }
@@ -151,15 +159,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWu,
                    const __grid_constant__ CUtensorMap tmX, Params p) {
   using LY = Layout<NMMA, SWIGLU>;
-  constexpr int S = LY::STAGES;
+  constexpr int SW = LY::SW;
+  constexpr int SX = LY::SX;
   constexpr int SLOT = slot_floats(NMMA, SWIGLU);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * LY::STAGE_BYTES);
-  uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* done = acc_empty + 1;
+  uint8_t* xring = smem + LY::X_RING;
+  uint64_t* full = reinterpret_cast<uint64_t*>(xring + SX * LY::X_BYTES);  // W ring [SW]
+  uint64_t* empty = full + SW;
+  uint64_t* fullx = empty + SW;  // x ring [SX]
+  uint64_t* emptyx = fullx + SX;
+  uint64_t* acc_full = emptyx + SX;  // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* done = acc_empty + 2;
   uint32_t* tmem_sm = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -171,12 +183,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int mcols = NORM ? p.M : (p.M < NMMA ? p.M : NMMA);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
+    for (int i = 0; i < SW; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    for (int i = 0; i < SX; ++i) {
+      mbar_init(&fullx[i], 1);
+      mbar_init(&emptyx[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
     mbar_init(done, 4);
     fence_barrier_init();
   }
@@ -195,43 +213,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
-    // ------------------------------ TMA producer ------------------------------
+    // --------------------------- weight TMA producer ---------------------------
+    // Weights never depend on the previous kernel on the stream, so this ring
+    // streams from the start, overlapping that kernel's tail (programmatic
+    // dependent launch).
     if (lane == 0) {
       tma_prefetch_desc(&tmW);
-      tma_prefetch_desc(&tmX);
       const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
-      // Weights never depend on the previous kernel on the stream: the first
-      // ring of W tiles is requested before waiting for it (programmatic
-      // dependent launch); x is loaded only after griddepcontrol.wait.
-      const long long pre_end = it_begin + S < it_end ? it_begin + S : it_end;
-      for (long long it = it_begin; it < pre_end; ++it) {
-        const int rb = (int)(it / p.KI);
-        const int k0 = (int)(it - (long long)rb * p.KI) * BK;
-        const int s = (int)(it - it_begin);
-        uint8_t* st = smem + s * LY::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], LY::TX);
-        tma_load_2d(st, &tmW, &full[s], k0, rb * BM, pol_w);
-        if (SWIGLU) tma_load_2d(st + WBOX, &tmWu, &full[s], k0, p.up_row_offset + rb * BM, pol_w);
-      }
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (long long it = it_begin; it < pre_end; ++it) {
-        const int k0 = (int)(it - (it / p.KI) * p.KI) * BK;
-        const int s = (int)(it - it_begin);
-        tma_load_2d(smem + s * LY::STAGE_BYTES + LY::X_OFF, &tmX, &full[s], k0, 0, pol_x);
-      }
-      int stage = (int)((pre_end - it_begin) % S);
-      uint32_t phase = (pre_end - it_begin) >= S ? 1u : 0u;
-      for (long long it = pre_end; it < it_end; ++it) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (long long it = it_begin; it < it_end; ++it) {
         const int rb = (int)(it / p.KI);
         const int k0 = (int)(it - (long long)rb * p.KI) * BK;
         if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) break;
-        uint8_t* st = smem + stage * LY::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[stage], LY::TX);
+        uint8_t* st = smem + stage * LY::W_BYTES;
+        mbar_arrive_expect_tx(&full[stage], LY::W_BYTES);
         tma_load_2d(st, &tmW, &full[stage], k0, rb * BM, pol_w);
         if (SWIGLU) tma_load_2d(st + WBOX, &tmWu, &full[stage], k0, p.up_row_offset + rb * BM, pol_w);
-        tma_load_2d(st + LY::X_OFF, &tmX, &full[stage], k0, 0, pol_x);
-        if (++stage == S) {
+        if (++stage == SW) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    __syncwarp();
+    return;
+  }
+
+  if (warp == 6) {
+    // ----------------------------- x TMA producer -----------------------------
+    // x is the previous kernel's output: loaded only after griddepcontrol.wait.
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      const uint64_t pol_x = l2_policy_evict_last();
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      for (long long it = it_begin; it < it_end; ++it) {
+        const int k0 = (int)(it % p.KI) * BK;
+        if (!mbar_wait(&emptyx[stage], phase ^ 1, p.err, kDevErrEmptyWait)) break;
+        mbar_arrive_expect_tx(&fullx[stage], LY::X_BYTES);
+        tma_load_2d(xring + stage * LY::X_BYTES, &tmX, &fullx[stage], k0, 0, pol_x);
+        if (++stage == SX) {
           stage = 0;
           phase ^= 1;
         }
@@ -244,49 +267,58 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
     constexpr uint32_t idesc = umma_idesc_bf16(NMMA);
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t acc_phase = 0;
+    int stage = 0, xstage = 0;
+    uint32_t phase = 0, xphase = 0;
+    int seg = 0;  // segment counter: buffer seg % NBUF, use (seg / NBUF)
     long long it = it_begin;
     bool ok = true;
     while (ok && it < it_end) {
       const int rb = (int)(it / p.KI);
       const long long seg_hi = min(it_end, (long long)(rb + 1) * p.KI);
-      if (!mbar_wait(acc_empty, acc_phase ^ 1, p.err, kDevErrMmaWait)) {
+      const int buf = seg % LY::NBUF;
+      const uint32_t use_par = (uint32_t)((seg / LY::NBUF) & 1);
+      const uint32_t tacc = tmem + buf * LY::ACC_COLS;
+      if (!mbar_wait(&acc_empty[buf], use_par ^ 1, p.err, kDevErrMmaWait)) {
         ok = false;
         break;
       }
       tc_fence_after();
       bool first = true;
       for (; it < seg_hi; ++it) {
-        if (!mbar_wait(&full[stage], phase, p.err, kDevErrFullWait)) {
+        if (!mbar_wait(&full[stage], phase, p.err, kDevErrFullWait) ||
+            !mbar_wait(&fullx[xstage], xphase, p.err, kDevErrFullWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t sb = smem_u32(smem + stage * LY::STAGE_BYTES);
+          const uint32_t sb = smem_u32(smem + stage * LY::W_BYTES);
           const uint64_t da = umma_desc_sw128(sb);
-          const uint64_t db = umma_desc_sw128(sb + LY::X_OFF);
+          const uint64_t db = umma_desc_sw128(smem_u32(xring + xstage * LY::X_BYTES));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t acc = (first && kk == 0) ? 0u : 1u;
-            umma_bf16(tmem, da + 2 * kk, db + 2 * kk, idesc, acc);
-            if (SWIGLU) umma_bf16(tmem + NMMA, umma_desc_sw128(sb + WBOX) + 2 * kk, db + 2 * kk, idesc, acc);
+            umma_bf16(tacc, da + 2 * kk, db + 2 * kk, idesc, acc);
+            if (SWIGLU) umma_bf16(tacc + NMMA, umma_desc_sw128(sb + WBOX) + 2 * kk, db + 2 * kk, idesc, acc);
           }
           umma_commit(&empty[stage]);
+          umma_commit(&emptyx[xstage]);
         }
         __syncwarp();
         first = false;
-        if (++stage == S) {
+        if (++stage == SW) {
           stage = 0;
           phase ^= 1;
         }
+        if (++xstage == SX) {
+          xstage = 0;
+          xphase ^= 1;
+        }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(acc_full);
+      if (lane == 0) umma_commit(&acc_full[buf]);
       __syncwarp();
-      acc_phase ^= 1;
+      ++seg;
     }
     // Free TMEM only after the epilogue warps have read their last accumulator.
     mbar_wait(done, 0, p.err, kDevErrMmaWait);
@@ -299,18 +331,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int et = threadIdx.x - EPI_WARP0 * 32;  // 0..127
   const int q = warp & 3;                       // TMEM lane quarter of this warp
   const int row = 32 * q + lane;                // output feature within the row block
-  const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16);
+  const uint32_t trow0 = tmem + ((uint32_t)(32 * q) << 16);
   asm volatile("griddepcontrol.wait;" ::: "memory");  // writes only after the previous kernel completed
-  uint32_t acc_phase = 0;
+  int seg = 0;
   long long it = it_begin;
   while (it < it_end) {
+    const int buf = seg % LY::NBUF;
+    const uint32_t use_par = (uint32_t)((seg / LY::NBUF) & 1);
+    const uint32_t trow = trow0 + buf * LY::ACC_COLS;
+    ++seg;
     const int rb = (int)(it / p.KI);
     const long long seg_lo = it;
     const long long seg_hi = min(it_end, (long long)(rb + 1) * p.KI);
     it = seg_hi;
     const bool full_rb = (seg_lo == (long long)rb * p.KI) && (seg_hi == (long long)(rb + 1) * p.KI);
-    if (!mbar_wait(acc_full, acc_phase, p.err, kDevErrMmaWait)) break;
-    acc_phase ^= 1;
+    if (!mbar_wait(&acc_full[buf], use_par, p.err, kDevErrMmaWait)) break;
     tc_fence_after();
     if (et == 0) TC_TRACE(3 + 5 * (seg_lo != it_begin));
     const int col = rb * BM + row;
@@ -328,7 +363,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
       continue;
     }
 
@@ -349,7 +384,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(acc_empty);  // the MMA warp may start the next segment
+    if (lane == 0) mbar_arrive(&acc_empty[buf]);  // this buffer may be refilled
     if (et == 0) TC_TRACE(5 + 5 * (seg_lo != it_begin));
   }
   tc_fence_before();
