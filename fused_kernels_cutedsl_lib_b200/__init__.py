@@ -7,11 +7,13 @@ no CPU or eager fallback: if the library is missing, calls raise.
 from .cdsl_fn_utils import compile_cutedsl
 from .gemm import (
     Gemm4SM90,
+    LoraGemmSM90,
     RMSNormLinear1SM90,
     Swiglu2SM90,
     SwigluSM90,
     alloc_workspace,
     linear,
+    lora_linear,
     rmsnorm_linear,
     skinny_gemm,
     swiglu_gemm,
@@ -33,12 +35,14 @@ from .decoding_attention import (
 
 __all__ = [
     "Gemm4SM90",
+    "LoraGemmSM90",
     "RMSNormLinear1SM90",
     "Swiglu2SM90",
     "SwigluSM90",
     "alloc_workspace",
     "compile_cutedsl",
     "linear",
+    "lora_linear",
     "rmsnorm_linear",
     "skinny_gemm",
     "swiglu_gemm",

@@ -58,6 +58,20 @@ SIGNATURES: dict[str, tuple] = {
         [_p, ctypes.c_longlong, _c_int, _c_int, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p],
     ),
     "fk_dattn1": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
+    "fk_lora_linear": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p],
+    ),
+    "fk_linear_kv_append": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int,
+         _c_int, _c_int, _p, ctypes.c_size_t, _p],
+    ),
+    "fk_dec_attn_fwd_commit": (
+        _c_int,
+        [_p, ctypes.c_longlong, _p, _p, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_int, _c_int, _c_float, _p],
+    ),
     "fk_qkv_head_scatter": (_c_int, [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
     "fk_dec_attn_fwd_paged": (
         _c_int,

@@ -221,4 +221,55 @@ __device__ __forceinline__ uint32_t swz128(uint32_t base, int row, int chunk) {
   return base + row * 128 + (((chunk ^ row) & 7) << 4);
 }
 
+// ---- optional epilogue / operand extensions of the linear family -------------
+
+// KV-cache append fused into a projection's epilogue: output columns
+// [k_col, k_col + width) of token m are also written to row seqlens_in[m] of the
+// K cache, [v_col, v_col + width) to the V cache, and seqlens_next[m] receives
+// the advanced length (out of place: the lengths are read by every CTA).
+// Contiguous cache [M, cap, width] when block_table is null, else a block pool
+// [*, block_size, width] addressed through block_table[m, pos / block_size].
+struct KvAppend {
+  __nv_bfloat16* k_cache;  // null: no append
+  __nv_bfloat16* v_cache;
+  const int* seqlens_in;
+  int* seqlens_next;       // may be null
+  const int* block_table;
+  int k_col, v_col, width, cap, max_blocks, block_size;
+  int m_base;              // token index of the launch's first row (token-tiled launches)
+};
+
+__device__ __forceinline__ void kv_append_store(const KvAppend& a, int m_local, int col, __nv_bfloat16 v) {
+  if (a.k_cache == nullptr) return;
+  const int m = a.m_base + m_local;
+  __nv_bfloat16* base;
+  int rel;
+  if (col >= a.k_col && col < a.k_col + a.width) {
+    base = a.k_cache;
+    rel = col - a.k_col;
+  } else if (col >= a.v_col && col < a.v_col + a.width) {
+    base = a.v_cache;
+    rel = col - a.v_col;
+  } else {
+    return;
+  }
+  const int pos = __ldg(a.seqlens_in + m);
+  const bool ok = pos >= 0 && pos < a.cap;
+  if (base == a.k_cache && rel == 0 && a.seqlens_next) a.seqlens_next[m] = ok ? pos + 1 : pos;
+  if (!ok) return;
+  const size_t row = a.block_table
+                         ? (size_t)__ldg(a.block_table + (size_t)m * a.max_blocks + pos / a.block_size) *
+                                   a.block_size + pos % a.block_size
+                         : (size_t)m * a.cap + pos;
+  base[row * a.width + rel] = v;
+}
+
+// Extensions a linear call may carry besides its main operands.
+struct LinearExtras {
+  KvAppend kv;                 // kv.k_cache null: none
+  const void* lora_xa;         // [M, rank] bf16: x . A^T (null: no LoRA)
+  const void* lora_b;          // [N, rank] bf16
+  int lora_rank;               // multiple of 8
+};
+
 }  // namespace fk

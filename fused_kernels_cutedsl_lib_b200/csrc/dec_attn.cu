@@ -342,14 +342,18 @@ __global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ 
                                                       const int* __restrict__ seqlens,
                                                       __nv_bfloat16* __restrict__ out,
                                                       float* __restrict__ lse, int B, int Hq,
-                                                      int Lmax, int chunk) {
+                                                      int Lmax, int chunk, int* seqlens_commit) {
   // Launched as a programmatic dependent of pass 1: wait for its partials.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= B * Hq) return;
   const int b = row / Hq;
-  int L = min(max(__ldg(seqlens + b), 0), Lmax);
+  const int Lraw = __ldg(seqlens + b);
+  // Optional: publish the lengths this step used to another buffer (the
+  // caller's length array when a projection epilogue advanced them out of place).
+  if (seqlens_commit && row == b * Hq && lane == 0) seqlens_commit[b] = Lraw;
+  int L = min(max(Lraw, 0), Lmax);
   const int n = (L + chunk - 1) / chunk;
   const size_t plane = (size_t)B * Hq;
   float M = -INFINITY;
@@ -529,11 +533,11 @@ int fk_dec_attn_fwd_paged(const void* q, const void* k_pool, const void* v_pool,
                              head_dim, num_splits, stream);
 }
 
-int fk_dec_attn_combine(const float* o_partial, const float* lse_partial,
-                        const int32_t* cache_seqlens, void* out, float* lse, int batch,
-                        int max_seqlen, int num_heads_q, int head_dim, int num_splits,
-                        void* stream) {
+static int combine_impl(const float* o_partial, const float* lse_partial, const int32_t* cache_seqlens,
+                        int32_t* seqlens_commit, void* out, float* lse, int batch, int max_seqlen,
+                        int num_heads_q, int head_dim, int num_splits, void* stream) {
   FK_CHECK_ARG(o_partial && lse_partial && cache_seqlens && out && lse, "null tensor pointer");
+  FK_CHECK_ARG(seqlens_commit != (int32_t*)cache_seqlens, "seqlens_commit must not alias cache_seqlens");
   FK_CHECK_ARG(batch >= 1 && max_seqlen >= 1 && num_heads_q >= 1 && num_splits >= 1,
                "sizes must be positive");
   FK_CHECK_ARG(head_dim == attn::D, "head_dim must be 128");
@@ -552,9 +556,35 @@ int fk_dec_attn_combine(const float* o_partial, const float* lse_partial,
   cfg.numAttrs = 1;
   FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn::combine_kernel, o_partial, lse_partial, cache_seqlens,
                                    static_cast<__nv_bfloat16*>(out), lse, batch, num_heads_q, max_seqlen,
-                                   chunk));
+                                   chunk, seqlens_commit));
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
+}
+
+int fk_dec_attn_combine(const float* o_partial, const float* lse_partial,
+                        const int32_t* cache_seqlens, void* out, float* lse, int batch,
+                        int max_seqlen, int num_heads_q, int head_dim, int num_splits,
+                        void* stream) {
+  return combine_impl(o_partial, lse_partial, cache_seqlens, nullptr, out, lse, batch, max_seqlen, num_heads_q,
+                      head_dim, num_splits, stream);
+}
+
+int fk_dec_attn_fwd_commit(const void* q, long long q_batch_stride, const void* k_cache, const void* v_cache,
+                           const int32_t* block_table, const int32_t* cache_seqlens, int32_t* seqlens_commit,
+                           void* out, float* lse, float* o_partial, float* lse_partial, int batch, int max_seqlen,
+                           int block_size, int num_blocks, int num_heads_q, int num_heads_kv, int head_dim,
+                           int num_splits, float softmax_scale, void* stream) {
+  if (block_table) {
+    FK_CHECK_ARG(block_size >= 64 && block_size % 64 == 0, "block_size must be a positive multiple of 64");
+    FK_CHECK_ARG(max_seqlen % block_size == 0 && num_blocks >= 1,
+                 "paged cache: max_seqlen must be max_blocks_per_seq * block_size, num_blocks >= 1");
+  }
+  int rc = splitkv_fwd_impl(q, q_batch_stride, k_cache, v_cache, cache_seqlens, o_partial, lse_partial, batch,
+                            max_seqlen, num_heads_q, num_heads_kv, head_dim, num_splits, softmax_scale, stream,
+                            block_table, block_size, num_blocks);
+  if (rc) return rc;
+  return combine_impl(o_partial, lse_partial, cache_seqlens, seqlens_commit, out, lse, batch, max_seqlen,
+                      num_heads_q, head_dim, num_splits, stream);
 }
 
 int fk_dec_attn_fwd(const void* q, const void* k_cache, const void* v_cache,

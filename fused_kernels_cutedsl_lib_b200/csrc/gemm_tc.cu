@@ -10,13 +10,16 @@
 // (N_mma = tokens rounded up to 32/64/128/256), so the accumulator is 128 TMEM
 // lanes (output features) x N_mma columns (tokens). No cluster multicast.
 //
-// Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: W box {64 k, 128 rows} (+ the SwiGLU up rows)
-//               and x box {64 k, N_mma rows} per stage
+// Roles (224 threads, one CTA per SM):
+//   warp 0      weight TMA producer: W box {64 k, 128 rows} (+ the SwiGLU up
+//               rows) into a deep ring; starts before griddepcontrol.wait
+//   warp 6      token TMA producer: x box {64 k, N_mma rows} into a shallow
+//               ring (x is re-read from L2); starts after griddepcontrol.wait
 //   warp 1      allocates TMEM, one lane issues tcgen05.mma (4 x K=16 per
-//               stage) and tcgen05.commit to free stages / publish results;
-//               frees TMEM once the epilogue warps report done
-//   warps 2-5   epilogue: tcgen05.ld the accumulators 16 columns at a time,
+//               stage) and tcgen05.commit to free both rings' stages and to
+//               publish results; frees TMEM once the epilogue warps report done
+//   warps 2-5   epilogue: tcgen05.ld the accumulators 16 columns at a time
+//               (double-buffered in TMEM when two fit in 512 columns),
 //               RMSNorm scale, SwiGLU, residual, bf16 store
 // Work is split stream-K over (row block, k block): every CTA streams the same
 // number of weight bytes. Row blocks finished inside one CTA are written by the
@@ -84,6 +87,8 @@ struct Params {
   int Mp;             // RMSNorm: column offset of the lo half (tokens rounded up to 16)
   long long total;
   int G;
+  int KI_main;        // k blocks of x . W^T; blocks [KI_main, KI) are the LoRA segment
+  KvAppend kv;
   int starts[kMaxGrid + 1];  // starts[c] = c * total / G: first iteration of CTA c
 };
 
@@ -151,13 +156,15 @@ __device__ __forceinline__ void store_out(const Params& p, int m, int col, float
   float val = swiglu ? silu_f(g * rs) * (u * rs) : g * rs;
   const size_t off = (size_t)m * p.N + col;
   if (p.residual) val += __bfloat162float(p.residual[off]);
-  p.y[off] = __float2bfloat16_rn(val);
+  const __nv_bfloat16 out = __float2bfloat16_rn(val);
+  p.y[off] = out;
+  kv_append_store(p.kv, m, col, out);
 }
 
 template <int NMMA, bool SWIGLU, bool NORM>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWu,
-                   const __grid_constant__ CUtensorMap tmX, Params p) {
+                   const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmXa, Params p) {
   using LY = Layout<NMMA, SWIGLU>;
   constexpr int SW = LY::SW;
   constexpr int SX = LY::SX;
@@ -224,11 +231,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       uint32_t phase = 0;
       for (long long it = it_begin; it < it_end; ++it) {
         const int rb = (int)(it / p.KI);
-        const int k0 = (int)(it - (long long)rb * p.KI) * BK;
+        const int kb = (int)(it - (long long)rb * p.KI);
+        // LoRA (plain linear only): k blocks past KI_main read B from the tmWu slot.
+        const bool lora = !SWIGLU && kb >= p.KI_main;
+        const int k0 = (lora ? kb - p.KI_main : kb) * BK;
         if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) break;
         uint8_t* st = smem + stage * LY::W_BYTES;
         mbar_arrive_expect_tx(&full[stage], LY::W_BYTES);
-        tma_load_2d(st, &tmW, &full[stage], k0, rb * BM, pol_w);
+        tma_load_2d(st, lora ? &tmWu : &tmW, &full[stage], k0, rb * BM, pol_w);
         if (SWIGLU) tma_load_2d(st + WBOX, &tmWu, &full[stage], k0, p.up_row_offset + rb * BM, pol_w);
         if (++stage == SW) {
           stage = 0;
@@ -250,10 +260,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (long long it = it_begin; it < it_end; ++it) {
-        const int k0 = (int)(it % p.KI) * BK;
+        const int kb = (int)(it % p.KI);
+        const bool lora = kb >= p.KI_main;  // LoRA: x . A^T
+        const int k0 = (lora ? kb - p.KI_main : kb) * BK;
         if (!mbar_wait(&emptyx[stage], phase ^ 1, p.err, kDevErrEmptyWait)) break;
         mbar_arrive_expect_tx(&fullx[stage], LY::X_BYTES);
-        tma_load_2d(xring + stage * LY::X_BYTES, &tmX, &fullx[stage], k0, 0, pol_x);
+        tma_load_2d(xring + stage * LY::X_BYTES, lora ? &tmXa : &tmX, &fullx[stage], k0, 0, pol_x);
         if (++stage == SX) {
           stage = 0;
           phase ^= 1;
@@ -508,8 +520,8 @@ __global__ void __launch_bounds__(128) tc_reduce_kernel(Params p) {
 }
 
 template <int NMMA, bool SWIGLU, bool NORM>
-static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtensorMap& tmX, const Params& p,
-                  cudaStream_t stream) {
+static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtensorMap& tmX, const CUtensorMap& tmXa,
+                  const Params& p, cudaStream_t stream) {
   using LY = Layout<NMMA, SWIGLU>;
   static_assert(LY::STAGES >= 2, "stage does not fit");
   auto kern = gemm_tc_kernel<NMMA, SWIGLU, NORM>;
@@ -525,7 +537,7 @@ static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtenso
     g.stream = stream;
     g.attrs = attr;
     g.numAttrs = 1;
-    FK_CHECK_CUDA(cudaLaunchKernelEx(&g, kern, tmW, tmWu, tmX, p));
+    FK_CHECK_CUDA(cudaLaunchKernelEx(&g, kern, tmW, tmWu, tmX, tmXa, p));
   }
   // Reduction of split row blocks, as a programmatic dependent launch.
   cudaLaunchConfig_t cfg = {};
@@ -540,13 +552,13 @@ static int launch(const CUtensorMap& tmW, const CUtensorMap& tmWu, const CUtenso
 }
 
 template <bool SWIGLU, bool NORM>
-static int launch_n(int nmma, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const Params& p,
-                    cudaStream_t st) {
+static int launch_n(int nmma, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
+                    const Params& p, cudaStream_t st) {
   switch (nmma) {
-    case 32: return launch<32, SWIGLU, NORM>(a, b, c, p, st);
-    case 64: return launch<64, SWIGLU, NORM>(a, b, c, p, st);
-    case 128: return launch<128, SWIGLU, NORM>(a, b, c, p, st);
-    case 256: return launch<256, SWIGLU, NORM>(a, b, c, p, st);
+    case 32: return launch<32, SWIGLU, NORM>(a, b, c, d, p, st);
+    case 64: return launch<64, SWIGLU, NORM>(a, b, c, d, p, st);
+    case 128: return launch<128, SWIGLU, NORM>(a, b, c, d, p, st);
+    case 256: return launch<256, SWIGLU, NORM>(a, b, c, d, p, st);
     default: return fail(kErrUnsupported, "unsupported token tile");
   }
 }
@@ -577,8 +589,13 @@ size_t tc_workspace_bytes(int M, int N, int K, bool swiglu) {
 
 int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
               const void* residual, void* y, int M, int N, int K, float eps, void* workspace, size_t workspace_bytes,
-              cudaStream_t stream) {
+              cudaStream_t stream, const LinearExtras* ex) {
   FK_CHECK_ARG(x && w && y, "null tensor pointer");
+  const bool lora = ex && ex->lora_xa;
+  FK_CHECK_ARG(!lora || (!gamma && !w_up), "LoRA is supported on the plain linear only");
+  FK_CHECK_ARG(!lora || (ex->lora_b && ex->lora_rank >= 8 && ex->lora_rank % 8 == 0 &&
+                         ((uintptr_t)ex->lora_xa & 15) == 0 && ((uintptr_t)ex->lora_b & 15) == 0),
+               "LoRA: rank must be a positive multiple of 8 and xA / B 16-byte aligned");
   FK_CHECK_ARG(M >= 1 && N >= 1 && K >= 1, "sizes must be positive");
   FK_CHECK_ARG(K % 8 == 0, "K must be a multiple of 8 (16-byte rows for TMA)");
   FK_CHECK_ARG((N + 127) / 128 <= kMaxRowBlocks, "N too large: at most 4096 row blocks of 128");
@@ -596,8 +613,12 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ws + kCounterBytes);
   float* rstd = reinterpret_cast<float*>(ws + kCounterBytes + tc_xs_bytes(K));
   const int num_rb = (N + tc::BM - 1) / tc::BM;
-  const int KI = (K + tc::BK - 1) / tc::BK;
+  const int KI_main = (K + tc::BK - 1) / tc::BK;
+  const int KI = KI_main + (lora ? (ex->lora_rank + tc::BK - 1) / tc::BK : 0);
   tc::Params p;
+  p.KI_main = KI_main;
+  p.kv = {};
+  if (ex) p.kv = ex->kv;
   p.partials = reinterpret_cast<float*>(ws + kCounterBytes + tc_xs_bytes(K) + tc_rstd_bytes());
   p.err = err;
   p.N = N;
@@ -623,6 +644,12 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   if (sw) {
     const uint64_t udims[2] = {(uint64_t)K, (uint64_t)(up_row_offset + N)};
     rc = encode_tma(&tmWu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w_up), udims, strides, wbox,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  } else if (lora) {
+    const uint64_t bdims[2] = {(uint64_t)ex->lora_rank, (uint64_t)N};
+    const uint64_t bstr[1] = {(uint64_t)ex->lora_rank * 2};
+    rc = encode_tma(&tmWu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ex->lora_b), bdims, bstr, wbox,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
@@ -662,12 +689,23 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
     p.M = mt;
     p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * N;
     p.residual = residual ? static_cast<const __nv_bfloat16*>(residual) + (size_t)m0 * N : nullptr;
+    CUtensorMap tmXa = tmX;
+    if (lora) {
+      const uint64_t adims[2] = {(uint64_t)ex->lora_rank, (uint64_t)mt};
+      const uint64_t astr[1] = {(uint64_t)ex->lora_rank * 2};
+      rc = encode_tma(&tmXa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                      const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(ex->lora_xa) +
+                                                 (size_t)m0 * ex->lora_rank),
+                      adims, astr, xbox, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
+    p.kv.m_base = m0;
     if (sw)
-      rc = norm ? tc::launch_n<true, true>(nmma, tmW, tmWu, tmX, p, stream)
-                : tc::launch_n<true, false>(nmma, tmW, tmWu, tmX, p, stream);
+      rc = norm ? tc::launch_n<true, true>(nmma, tmW, tmWu, tmX, tmXa, p, stream)
+                : tc::launch_n<true, false>(nmma, tmW, tmWu, tmX, tmXa, p, stream);
     else
-      rc = norm ? tc::launch_n<false, true>(nmma, tmW, tmWu, tmX, p, stream)
-                : tc::launch_n<false, false>(nmma, tmW, tmWu, tmX, p, stream);
+      rc = norm ? tc::launch_n<false, true>(nmma, tmW, tmWu, tmX, tmXa, p, stream)
+                : tc::launch_n<false, false>(nmma, tmW, tmWu, tmX, tmXa, p, stream);
     if (rc) return rc;
   }
   return kOk;

@@ -8,24 +8,26 @@ namespace fk {
 size_t skinny_workspace_bytes(int N, int G, bool swiglu);
 int skinny_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
                   const void* residual, void* y, int M, int N, int K, float eps, void* workspace,
-                  size_t workspace_bytes, int grid_override, cudaStream_t stream);
+                  size_t workspace_bytes, int grid_override, cudaStream_t stream,
+                  const LinearExtras* ex = nullptr);
 size_t tc_workspace_bytes(int M, int N, int K, bool swiglu);
 int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
               const void* residual, void* y, int M, int N, int K, float eps, void* workspace,
-              size_t workspace_bytes, cudaStream_t stream);
+              size_t workspace_bytes, cudaStream_t stream, const LinearExtras* ex = nullptr);
 }  // namespace fk
 
 using namespace fk;
 
 static int dispatch(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
                     const void* residual, void* y, int M, int N, int K, float eps, void* workspace,
-                    size_t workspace_bytes, void* stream) {
+                    size_t workspace_bytes, void* stream, const LinearExtras* ex = nullptr) {
   FK_CHECK_ARG(M >= 1, "M must be >= 1");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (M <= 16)
     return skinny_linear(x, gamma, w, w_up, up_row_offset, residual, y, M, N, K, eps, workspace,
-                         workspace_bytes, 0, st);
-  return tc_linear(x, gamma, w, w_up, up_row_offset, residual, y, M, N, K, eps, workspace, workspace_bytes, st);
+                         workspace_bytes, 0, st, ex);
+  return tc_linear(x, gamma, w, w_up, up_row_offset, residual, y, M, N, K, eps, workspace, workspace_bytes, st,
+                   ex);
 }
 
 extern "C" {
@@ -77,6 +79,49 @@ int fk_rmsnorm_swiglu(const void* x, const void* gamma, const void* w_gate_up, v
   FK_CHECK_ARG(gamma != nullptr && w_gate_up != nullptr, "null tensor pointer");
   return dispatch(x, gamma, w_gate_up, w_gate_up, N, nullptr, y, M, N, K, eps, workspace, workspace_bytes,
                   stream);
+}
+
+// LoRA linear: y = x . W^T + xA . B^T (+ residual), xA = x . A^T given [M, rank].
+// The LoRA product runs as extra k blocks of the same GEMM ([x | xA] . [W | B]^T),
+// accumulated in fp32 with the main product before the single bf16 rounding.
+int fk_lora_linear(const void* x, const void* w, const void* lora_xa, const void* lora_b, const void* residual,
+                   void* y, int M, int N, int K, int rank, void* workspace, size_t workspace_bytes, void* stream) {
+  FK_CHECK_ARG(lora_xa != nullptr && lora_b != nullptr, "lora_xa / lora_b is null");
+  LinearExtras ex = {};
+  ex.lora_xa = lora_xa;
+  ex.lora_b = lora_b;
+  ex.lora_rank = rank;
+  return dispatch(x, nullptr, w, nullptr, 0, residual, y, M, N, K, 0.f, workspace, workspace_bytes, stream, &ex);
+}
+
+// Projection with the KV-cache append in its epilogue (gamma null: plain linear).
+int fk_linear_kv_append(const void* x, const void* gamma, const void* w, void* y, int M, int N, int K, float eps,
+                        void* k_cache, void* v_cache, const int32_t* block_table, const int32_t* cache_seqlens,
+                        int32_t* seqlens_next, int k_col, int v_col, int num_heads_kv, int head_dim,
+                        int max_seqlen, int block_size, void* workspace, size_t workspace_bytes, void* stream) {
+  FK_CHECK_ARG(k_cache && v_cache && cache_seqlens, "null cache / length pointer");
+  FK_CHECK_ARG(num_heads_kv >= 1 && head_dim >= 1 && max_seqlen >= 1, "sizes must be positive");
+  const long long width = (long long)num_heads_kv * head_dim;
+  FK_CHECK_ARG(k_col >= 0 && v_col >= 0 && k_col + width <= N && v_col + width <= N,
+               "K / V column ranges must lie inside the N output columns");
+  FK_CHECK_ARG(k_col + width <= v_col || v_col + width <= k_col, "K and V column ranges overlap");
+  FK_CHECK_ARG(seqlens_next != (int32_t*)cache_seqlens,
+               "seqlens_next must not alias cache_seqlens (every CTA reads the lengths)");
+  FK_CHECK_ARG(!block_table || (block_size >= 1 && max_seqlen % block_size == 0),
+               "paged cache: max_seqlen must be max_blocks_per_seq * block_size");
+  LinearExtras ex = {};
+  ex.kv.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  ex.kv.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  ex.kv.seqlens_in = cache_seqlens;
+  ex.kv.seqlens_next = seqlens_next;
+  ex.kv.block_table = block_table;
+  ex.kv.k_col = k_col;
+  ex.kv.v_col = v_col;
+  ex.kv.width = (int)width;
+  ex.kv.cap = max_seqlen;
+  ex.kv.block_size = block_table ? block_size : max_seqlen;
+  ex.kv.max_blocks = block_table ? max_seqlen / block_size : 1;
+  return dispatch(x, gamma, w, nullptr, 0, nullptr, y, M, N, K, eps, workspace, workspace_bytes, stream, &ex);
 }
 
 }  // extern "C"

@@ -29,7 +29,8 @@
 namespace fk {
 int skinny_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
                   const void* residual, void* y, int M, int N, int K, float eps, void* workspace,
-                  size_t workspace_bytes, int grid_override, cudaStream_t stream);
+                  size_t workspace_bytes, int grid_override, cudaStream_t stream,
+                  const LinearExtras* ex = nullptr);
 size_t skinny_workspace_bytes(int N, int G, bool swiglu);
 }  // namespace fk
 

@@ -76,9 +76,11 @@ struct Params {
   float* partials;                // [2 * G][slot_floats]
   int* err;
   int M, N, K, KI, num_rb, up_row_offset;
+  int KI_main;                    // k blocks of x . W^T; blocks [KI_main, KI) are the LoRA segment
   long long total;                // num_rb * KI
   int G;
   float eps, inv_k;
+  KvAppend kv;
 };
 
 __device__ __forceinline__ long long it_start(const Params& p, int c) {
@@ -129,23 +131,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (NORM) tma_prefetch_desc(&tmG);
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
+      // LoRA (plain linear only): k blocks past KI_main read B (in the tmWu slot)
+      // and x . A^T (in the tmG slot) instead of W and x; the zero fill past
+      // the rank makes the extra columns contribute nothing.
       auto load_w = [&](int s, long long it) {
         const int rb = (int)(it / p.KI);
-        const int k0 = (int)(it - (long long)rb * p.KI) * KT;
+        const int kb = (int)(it - (long long)rb * p.KI);
+        const bool lora = !SWIGLU && !NORM && kb >= p.KI_main;
+        const CUtensorMap* wm = lora ? &tmWu : &tmW;
+        const int k0 = (lora ? kb - p.KI_main : kb) * KT;
         uint8_t* st = smem + s * LY::STAGE_BYTES;
         mbar_arrive_expect_tx(&full[s], LY::TX_BYTES);
-        tma_load_2d(st, &tmW, &full[s], k0, rb * RB, pol_w);
-        tma_load_2d(st + WBOX_BYTES, &tmW, &full[s], k0 + 64, rb * RB, pol_w);
+        tma_load_2d(st, wm, &full[s], k0, rb * RB, pol_w);
+        tma_load_2d(st + WBOX_BYTES, wm, &full[s], k0 + 64, rb * RB, pol_w);
         if (SWIGLU) {
           tma_load_2d(st + WTILE_BYTES, &tmWu, &full[s], k0, p.up_row_offset + rb * RB, pol_w);
           tma_load_2d(st + WTILE_BYTES + WBOX_BYTES, &tmWu, &full[s], k0 + 64, p.up_row_offset + rb * RB, pol_w);
         }
       };
       auto load_x = [&](int s, long long it) {
-        const int k0 = (int)(it % p.KI) * KT;
+        const int kb = (int)(it % p.KI);
+        const bool lora = !SWIGLU && !NORM && kb >= p.KI_main;
+        const CUtensorMap* xm = lora ? &tmG : &tmX;
+        const int k0 = (lora ? kb - p.KI_main : kb) * KT;
         uint8_t* st = smem + s * LY::STAGE_BYTES;
-        tma_load_2d(st + LY::X_OFF, &tmX, &full[s], k0, 0, pol_x);
-        tma_load_2d(st + LY::X_OFF + LY::XBOX_BYTES, &tmX, &full[s], k0 + 64, 0, pol_x);
+        tma_load_2d(st + LY::X_OFF, xm, &full[s], k0, 0, pol_x);
+        tma_load_2d(st + LY::X_OFF + LY::XBOX_BYTES, xm, &full[s], k0 + 64, 0, pol_x);
         if (NORM) {
           asm volatile(
               "cp.async.bulk.tensor.1d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
@@ -407,7 +418,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float val = SWIGLU ? silu_f(v[0][t][e]) * v[NMAT - 1][t][e] : v[0][t][e];
             const size_t off = (size_t)m * p.N + col;
             if (p.residual) val += __bfloat162float(p.residual[off]);
-            p.y[off] = __float2bfloat16_rn(val);
+            const __nv_bfloat16 out = __float2bfloat16_rn(val);
+            p.y[off] = out;
+            kv_append_store(p.kv, m, col, out);
           }
         }
     }
@@ -450,9 +463,14 @@ size_t skinny_workspace_bytes(int N, int G, bool swiglu) {
 // Shared entry used by every skinny-path C function. `w_up` null => no SwiGLU.
 int skinny_linear(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
                   const void* residual, void* y, int M, int N, int K, float eps, void* workspace,
-                  size_t workspace_bytes, int grid_override, cudaStream_t stream) {
+                  size_t workspace_bytes, int grid_override, cudaStream_t stream, const LinearExtras* ex) {
   FK_CHECK_ARG(x && w && y, "null tensor pointer");
   FK_CHECK_ARG(M >= 1 && M <= sk::MAXM, "skinny path takes 1 <= M <= 16");
+  const bool lora = ex && ex->lora_xa;
+  FK_CHECK_ARG(!lora || (!gamma && !w_up), "LoRA is supported on the plain linear only");
+  FK_CHECK_ARG(!lora || (ex->lora_b && ex->lora_rank >= 8 && ex->lora_rank % 8 == 0 &&
+                         ((uintptr_t)ex->lora_xa & 15) == 0 && ((uintptr_t)ex->lora_b & 15) == 0),
+               "LoRA: rank must be a positive multiple of 8 and xA / B 16-byte aligned");
   FK_CHECK_ARG(N >= 1 && K >= 1, "N and K must be positive");
   FK_CHECK_ARG(K % 8 == 0, "K must be a multiple of 8 (16-byte rows for TMA)");
   FK_CHECK_ARG((N + 127) / 128 <= kMaxRowBlocks, "N too large: at most 4096 row blocks of 128");
@@ -463,7 +481,9 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   const bool sw = w_up != nullptr;
   const bool norm = gamma != nullptr;
   const int num_rb0 = (N + sk::RB - 1) / sk::RB;
-  const long long total0 = (long long)num_rb0 * ((K + sk::KT - 1) / sk::KT);
+  const int KI_main = (K + sk::KT - 1) / sk::KT;
+  const int KI_all = KI_main + (lora ? (ex->lora_rank + sk::KT - 1) / sk::KT : 0);
+  const long long total0 = (long long)num_rb0 * KI_all;
   int G = grid_override > 0 ? grid_override : num_sms();
   if ((long long)G > total0) G = (int)total0;
   FK_CHECK_ARG(workspace_bytes >= skinny_workspace_bytes(N, G, sw), "workspace too small");
@@ -480,7 +500,13 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   p.M = M;
   p.N = N;
   p.K = K;
-  p.KI = (K + sk::KT - 1) / sk::KT;
+  p.KI = KI_all;
+  p.KI_main = KI_main;
+  p.kv = {};
+  if (ex) {
+    p.kv = ex->kv;
+    p.kv.m_base = 0;
+  }
   p.num_rb = num_rb;
   p.up_row_offset = up_row_offset;
   p.total = (long long)num_rb * p.KI;
@@ -510,7 +536,18 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
     rc = encode_tma(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, strides, xbox,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    if (norm) {
+    if (lora) {
+      const int r = ex->lora_rank;
+      const uint64_t bdims[2] = {(uint64_t)r, (uint64_t)N};
+      const uint64_t bstr[1] = {(uint64_t)r * 2};
+      rc = encode_tma(&tmWu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ex->lora_b), bdims, bstr, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      const uint64_t adims[2] = {(uint64_t)r, (uint64_t)M};
+      rc = encode_tma(&tmG, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ex->lora_xa), adims, bstr, xbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    } else if (norm) {
       const uint64_t gdims[1] = {(uint64_t)K};
       const uint32_t gbox[1] = {(uint32_t)sk::KT};
       rc = encode_tma(&tmG, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 1, const_cast<void*>(gamma), gdims, nullptr, gbox,

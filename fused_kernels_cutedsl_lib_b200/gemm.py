@@ -9,6 +9,9 @@ tuning arguments and called on caller-allocated tensors, returning ``None``:
   (python/cutedsl_kernels/rmsnorm_linear/attempt1/gemm.py:52-65,136-170)
 * ``Swiglu2SM90(...)(a, b, b1, c)`` — ``c = silu(a @ b.t()) * (a @ b1.t())``
   (python/cutedsl_kernels/swiglu/attempt1/gemm2.py:69-81,145-187)
+* ``GemmSM90(...)(a, b, lora_xA, lora_B, c, stream)`` of the LoRA kernel —
+  ``c = a @ b.t() + lora_xA @ lora_B.t()``
+  (python/cutedsl_kernels/lora/attempt1/gemm.py:57-178; check :672-675)
 
 The same class names are provided here. Their Hopper tuning arguments (tile
 shapes, cluster shapes, stage counts) are accepted and ignored: the B200
@@ -146,6 +149,53 @@ def swiglu_gemm2(x, w_gate, w_up, out=None, *, workspace=None, stream=None):
     return linear(x, w_gate, out, w_up=w_up, up_row_offset=0, workspace=workspace, stream=stream)
 
 
+def lora_linear(x, w, lora_b, out=None, *, lora_a=None, lora_xa=None, residual=None, workspace=None,
+                stream=None):
+    """``out = x @ w.t() + (x @ lora_a.t()) @ lora_b.t()`` (+ ``residual``).
+
+    Give either ``lora_a`` [rank, K] (``x @ lora_a.t()`` is then computed with
+    :func:`linear`, as the reference computes its ``lora_xA`` operand before the
+    call, lora/attempt1/gemm.py:700-704) or the precomputed ``lora_xa`` [M, rank].
+    The low-rank product is accumulated in the same fp32 accumulator as the main
+    product (extra k blocks of one GEMM) and rounded once.
+    """
+    _check_x_w(x, w)
+    M, K = x.shape
+    N = w.shape[0]
+    require_tensor("lora_b", lora_b, torch.bfloat16, 2)
+    if lora_b.shape[0] != N:
+        raise ValueError(f"lora_b must be [N={N}, rank], got {tuple(lora_b.shape)}")
+    r = lora_b.shape[1]
+    if r < 8 or r % 8:
+        raise ValueError(f"LoRA rank must be a positive multiple of 8, got {r}")
+    if (lora_a is None) == (lora_xa is None):
+        raise ValueError("give exactly one of lora_a and lora_xa")
+    if lora_xa is None:
+        require_tensor("lora_a", lora_a, torch.bfloat16, 2)
+        if tuple(lora_a.shape) != (r, K):
+            raise ValueError(f"lora_a must be [{r}, {K}], got {tuple(lora_a.shape)}")
+        lora_xa = linear(x, lora_a, workspace=workspace, stream=stream)
+    require_tensor("lora_xa", lora_xa, torch.bfloat16, 2)
+    if tuple(lora_xa.shape) != (M, r):
+        raise ValueError(f"lora_xa must be [{M}, {r}], got {tuple(lora_xa.shape)}")
+    dev = x.device
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    _check_out(out, M, N)
+    if residual is not None:
+        _check_out(residual, M, N, "residual")
+    same_device(*[t for t in (x, w, lora_b, lora_xa, residual, out) if t is not None])
+    st = stream_for(dev, stream)
+    need = workspace_bytes(M, N, K)
+    ws = workspace if workspace is not None else workspace_for(need, dev)
+    if ws.numel() * ws.element_size() < need:
+        raise ValueError(f"workspace holds {ws.numel() * ws.element_size()} bytes, needs {need}")
+    _native.check(_native.load().fk_lora_linear(
+        ptr(x), ptr(w), ptr(lora_xa), ptr(lora_b), ptr(residual) if residual is not None else None, ptr(out),
+        M, N, K, r, ptr(ws), ws.numel() * ws.element_size(), st))
+    return out
+
+
 _ones_cache: dict = {}
 
 
@@ -194,3 +244,15 @@ class Swiglu2SM90:
 
 
 SwigluSM90 = Swiglu2SM90
+
+
+class LoraGemmSM90:
+    """LoRA ``GemmSM90(**tuning)(a, b, lora_xA, lora_B, c, stream)``:
+    ``c = a @ b.t() + lora_xA @ lora_B.t()`` (lora/attempt1/gemm.py:57-178;
+    tuning arguments accepted, unused)."""
+
+    def __init__(self, *args, **kwargs):
+        self.tuning = (args, kwargs)
+
+    def __call__(self, a, b, lora_xA, lora_B, c, stream=None):
+        lora_linear(a, b, lora_B, c, lora_xa=lora_xA, stream=stream)

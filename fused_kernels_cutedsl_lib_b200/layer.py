@@ -29,7 +29,7 @@ import torch
 from . import _native
 from ._tensors import ptr, stream_for
 from .decoding_attention import alloc_partials, default_num_splits
-from .gemm import alloc_workspace, linear, workspace_bytes
+from .gemm import alloc_workspace, linear, workspace_bytes, workspace_for
 from .sharding import column_range, shard_gate_up
 
 HEAD_DIM = 128
@@ -102,6 +102,52 @@ def attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_partial
         ptr(o_partial), ptr(lse_partial), B, L, num_heads_q, num_heads_kv, HEAD_DIM, num_splits, scale, st))
 
 
+def linear_kv_append(x, w, out, k_cache, v_cache, cache_seqlens, seqlens_next, num_heads_q, num_heads_kv, *,
+                     gamma=None, eps=1e-6, block_table=None, workspace=None, stream=None):
+    """QKV projection (RMSNorm-fused when ``gamma`` is given) whose epilogue also
+    writes the new K/V rows into the caches at ``cache_seqlens[b]`` and the
+    advanced lengths into ``seqlens_next`` (a different tensor). With
+    ``block_table`` the caches are block pools ``[num_blocks, block_size, Hkv, D]``."""
+    M, K = x.shape
+    N = w.shape[0]
+    if seqlens_next is not None and seqlens_next.data_ptr() == cache_seqlens.data_ptr():
+        raise ValueError("seqlens_next must not alias cache_seqlens")
+    if block_table is not None:
+        cap = block_table.shape[1] * k_cache.shape[1]
+        bs = k_cache.shape[1]
+    else:
+        cap, bs = k_cache.shape[1], 0
+    dev = x.device
+    st = stream_for(dev, stream)
+    need = workspace_bytes(M, N, K)
+    ws = workspace if workspace is not None else workspace_for(need, dev)
+    _native.check(_native.load().fk_linear_kv_append(
+        ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(out), M, N, K, float(eps),
+        ptr(k_cache), ptr(v_cache), ptr(block_table) if block_table is not None else None, ptr(cache_seqlens),
+        ptr(seqlens_next) if seqlens_next is not None else None, num_heads_q * HEAD_DIM,
+        (num_heads_q + num_heads_kv) * HEAD_DIM, num_heads_kv, HEAD_DIM, cap, bs, ptr(ws),
+        ws.numel() * ws.element_size(), st))
+    return out
+
+
+def attention_commit(qkv, k_cache, v_cache, cache_seqlens, seqlens_commit, out, lse, o_partial, lse_partial,
+                     num_splits, num_heads_q, num_heads_kv, *, block_table=None, softmax_scale=None, stream=None):
+    """:func:`attention_from_qkv` that also copies the lengths it used into
+    ``seqlens_commit`` (pass 2 writes them; a different tensor from ``cache_seqlens``)."""
+    B = qkv.shape[0]
+    if block_table is not None:
+        bs = k_cache.shape[1]
+        L, nblk = block_table.shape[1] * bs, k_cache.shape[0]
+    else:
+        L, bs, nblk = k_cache.shape[1], 0, 0
+    scale = 1.0 / math.sqrt(HEAD_DIM) if softmax_scale is None else float(softmax_scale)
+    st = stream_for(qkv.device, stream)
+    _native.check(_native.load().fk_dec_attn_fwd_commit(
+        ptr(qkv), qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(block_table) if block_table is not None else None,
+        ptr(cache_seqlens), ptr(seqlens_commit), ptr(out), ptr(lse), ptr(o_partial), ptr(lse_partial), B, L, bs,
+        nblk, num_heads_q, num_heads_kv, HEAD_DIM, num_splits, scale, st))
+
+
 class DecodeLayer:
     """Single-GPU decode step. ``layer(x, k_cache, v_cache, cache_seqlens) -> y``.
 
@@ -111,7 +157,9 @@ class DecodeLayer:
     nothing and the step can be replayed inside a CUDA graph.
     """
 
-    def __init__(self, weights: LayerWeights, num_heads_q=32, num_heads_kv=8, eps=1e-6, num_splits=None):
+    def __init__(self, weights: LayerWeights, num_heads_q=32, num_heads_kv=8, eps=1e-6, num_splits=None,
+                 fuse_append=True):
+        self.fuse_append = fuse_append  # KV append in the QKV epilogue (else a separate append kernel)
         self.w = weights
         self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
         self.num_splits = num_splits
@@ -134,7 +182,8 @@ class DecodeLayer:
                      qkv=torch.empty(B, self.qkv_dim, **bf), attn=torch.empty(B, self.hq * HEAD_DIM, **bf),
                      lse=torch.empty(B, self.hq, dtype=torch.float32, device=device),
                      h=torch.empty(B, self.hidden, **bf), gu=torch.empty(B, self.ffn, **bf),
-                     y=torch.empty(B, self.hidden, **bf))
+                     y=torch.empty(B, self.hidden, **bf),
+                     lens_next=torch.empty(B, dtype=torch.int32, device=device))
             self._bufs[key] = b
         return b
 
@@ -142,10 +191,18 @@ class DecodeLayer:
         B, L = x.shape[0], k_cache.shape[1]
         b = self.buffers(B, L, x.device)
         w, ws = self.w, b["ws"]
-        linear(x, w.w_qkv, b["qkv"], gamma=w.gamma_attn, eps=self.eps, workspace=ws, stream=stream)
-        kv_append(b["qkv"], k_cache, v_cache, cache_seqlens, self.hq, self.hkv, stream=stream)
-        attention_from_qkv(b["qkv"], k_cache, v_cache, cache_seqlens, b["attn"], b["lse"], b["o_p"], b["l_p"],
-                           b["S"], self.hq, self.hkv, stream=stream)
+        if self.fuse_append:
+            # QKV epilogue appends K/V and writes the advanced lengths to lens_next;
+            # attention reads lens_next and publishes it back to cache_seqlens.
+            linear_kv_append(x, w.w_qkv, b["qkv"], k_cache, v_cache, cache_seqlens, b["lens_next"], self.hq,
+                             self.hkv, gamma=w.gamma_attn, eps=self.eps, workspace=ws, stream=stream)
+            attention_commit(b["qkv"], k_cache, v_cache, b["lens_next"], cache_seqlens, b["attn"], b["lse"],
+                             b["o_p"], b["l_p"], b["S"], self.hq, self.hkv, stream=stream)
+        else:
+            linear(x, w.w_qkv, b["qkv"], gamma=w.gamma_attn, eps=self.eps, workspace=ws, stream=stream)
+            kv_append(b["qkv"], k_cache, v_cache, cache_seqlens, self.hq, self.hkv, stream=stream)
+            attention_from_qkv(b["qkv"], k_cache, v_cache, cache_seqlens, b["attn"], b["lse"], b["o_p"], b["l_p"],
+                               b["S"], self.hq, self.hkv, stream=stream)
         linear(b["attn"], w.w_o, b["h"], residual=x, workspace=ws, stream=stream)
         linear(b["h"], w.w_gate_up, b["gu"], gamma=w.gamma_ffn, eps=self.eps, w_up=w.w_gate_up,
                up_row_offset=self.ffn, workspace=ws, stream=stream)

@@ -4,6 +4,7 @@ functions take torch tensors directly, as the reference's compiled kernels do
 
 Functions: ``dec_attn_splitkv_fwd``, ``dec_attn_combine``, ``dattn1``,
 ``skinny_gemm``, ``rmsnorm_linear``, ``swiglu_gemm``, ``swiglu_gemm2``,
+``lora_gemm`` (the LoRA kernel's ``(a, b, lora_xA, lora_B, c)`` plus workspace),
 ``linear_workspace_bytes`` (same arguments and meaning as the C ABI in
 include/fk_b200.h, with tensors in place of pointer + size lists). They run
 on the tensors' current stream and write caller-allocated outputs.

@@ -108,6 +108,14 @@ void swiglu_gemm2(TensorView x, TensorView b, TensorView b1, TensorView y, Tenso
                         (int)x.size(1), workspace.data_ptr(), nbytes(workspace), stream_of(x)));
 }
 
+// LoRA GEMM with the reference's call shape (a, b, lora_xA, lora_B, c): c = a b^T + lora_xA lora_B^T.
+void lora_gemm(TensorView x, TensorView w, TensorView lora_xa, TensorView lora_b, TensorView y, TensorView workspace) {
+  use(x);
+  check(fk_lora_linear(x.data_ptr(), w.data_ptr(), lora_xa.data_ptr(), lora_b.data_ptr(), nullptr, y.data_ptr(),
+                       (int)x.size(0), (int)w.size(0), (int)x.size(1), (int)lora_b.size(1), workspace.data_ptr(),
+                       nbytes(workspace), stream_of(x)));
+}
+
 int64_t linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t swiglu) {
   size_t b = 0;
   check(fk_linear_workspace_bytes((int)M, (int)N, (int)K, swiglu ? FK_LINEAR_SWIGLU : 0, &b));
@@ -123,4 +131,5 @@ TVM_FFI_DLL_EXPORT_TYPED_FUNC(skinny_gemm, skinny_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(rmsnorm_linear, rmsnorm_linear);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm, swiglu_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm2, swiglu_gemm2);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(lora_gemm, lora_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(linear_workspace_bytes, linear_workspace_bytes);

@@ -118,6 +118,20 @@ FK_API int fk_dec_attn_fwd_paged(const void* q, const void* k_pool, const void* 
                                  int block_size, int num_blocks, int num_heads_q, int num_heads_kv, int head_dim,
                                  int num_splits, float softmax_scale, void* stream);
 
+/* Both passes (contiguous cache, or paged when block_table is non-null:
+ * max_seqlen = max_blocks_per_seq * block_size, num_blocks in the pool), q at
+ * a row stride, and pass 2 also writes the lengths it used to
+ * seqlens_commit[b] (a different array from cache_seqlens). Used after
+ * fk_linear_kv_append advanced the lengths into a scratch array: attention
+ * reads the scratch and publishes it to the caller's length array, so the
+ * decode step needs no separate append or copy kernel. */
+FK_API int fk_dec_attn_fwd_commit(const void* q, long long q_batch_stride, const void* k_cache,
+                                  const void* v_cache, const int32_t* block_table, const int32_t* cache_seqlens,
+                                  int32_t* seqlens_commit, void* out, float* lse, float* o_partial,
+                                  float* lse_partial, int batch, int max_seqlen, int block_size, int num_blocks,
+                                  int num_heads_q, int num_heads_kv, int head_dim, int num_splits,
+                                  float softmax_scale, void* stream);
+
 /* Paged form of fk_kv_append: the new row of b goes to block
  * block_table[b][len / block_size], row len % block_size (any block_size >= 1). */
 FK_API int fk_kv_append_paged(const void* src, long long src_row_stride, int k_col, int v_col, void* k_pool,
@@ -205,6 +219,32 @@ FK_API int fk_swiglu_gemm2(const void* x, const void* w_gate, const void* w_up, 
 FK_API int fk_rmsnorm_swiglu(const void* x, const void* gamma, const void* w_gate_up, void* y,
                              int M, int N, int K, float eps, void* workspace,
                              size_t workspace_bytes, void* stream);
+
+/* LoRA linear: y[M, N] = x W^T + xA B^T (+ residual when non-null), with
+ * xA = x A^T given as [M, rank] and B as [N, rank] (rank a multiple of 8).
+ * Replaces GemmSM90(...)(a, b, lora_xA, lora_B, c, stream) of
+ * python/cutedsl_kernels/lora/attempt1/gemm.py:136-178 (check :672-675:
+ * (a @ b.t()) + (a @ lA.t() @ lB.t())). The low-rank term is extra k blocks
+ * of the same accumulation, rounded to bf16 once. Workspace as fk_linear. */
+FK_API int fk_lora_linear(const void* x, const void* w, const void* lora_xa, const void* lora_b,
+                          const void* residual, void* y, int M, int N, int K, int rank, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Projection (RMSNorm -> linear when gamma is non-null, else plain) whose
+ * epilogue also appends the new K/V rows to the cache: output columns
+ * [k_col, k_col + num_heads_kv*head_dim) of token m go to the K cache at
+ * position cache_seqlens[m], [v_col, ...) to the V cache, and seqlens_next[m]
+ * (a different array from cache_seqlens, may be null) receives the advanced
+ * length; rows already at max_seqlen keep their length and are not written.
+ * block_table null: caches [M, max_seqlen, Hkv, D]; else block pools
+ * [*, block_size, Hkv, D] with max_seqlen = max_blocks_per_seq * block_size.
+ * The fused form of DAttn2's projection + cache write
+ * (python/cutedsl_kernels/decoding_attention/attempt2.py:98-302, write :276-286). */
+FK_API int fk_linear_kv_append(const void* x, const void* gamma, const void* w, void* y, int M, int N, int K,
+                               float eps, void* k_cache, void* v_cache, const int32_t* block_table,
+                               const int32_t* cache_seqlens, int32_t* seqlens_next, int k_col, int v_col,
+                               int num_heads_kv, int head_dim, int max_seqlen, int block_size, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* Skinny GEMM y = x W^T (1 <= M <= 16, N <= 524288) that allocates nothing:
  * its stream-K scratch is a fixed ~2.7 MB device array inside this library

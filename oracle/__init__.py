@@ -17,6 +17,7 @@ from .ops import (
     decode_attention,
     decode_layer,
     linear,
+    lora_linear,
     rmsnorm,
     rmsnorm_linear,
     silu,
@@ -28,6 +29,7 @@ __all__ = [
     "dattn1_reference",
     "decode_attention",
     "decode_layer",
+    "lora_linear",
     "linear",
     "rmsnorm",
     "rmsnorm_linear",

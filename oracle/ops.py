@@ -107,6 +107,18 @@ def swiglu_separate(x, b, b1):
     return silu(xf @ _cpu32(b).t()) * (xf @ _cpu32(b1).t())
 
 
+def lora_linear(x, w, lora_a, lora_b, lora_xa=None):
+    """``(a @ b.t()) + (a @ lA.t() @ lB.t())`` in fp32 (lora/attempt1/gemm.py:672-675).
+
+    The reference kernel takes ``lora_xA = a @ lA.t()`` precomputed by torch
+    (gemm.py:700-704); pass that bf16 tensor as ``lora_xa`` to check a kernel
+    that was given the same operand.
+    """
+    xf = _cpu32(x)
+    xa = _cpu32(lora_xa) if lora_xa is not None else xf @ _cpu32(lora_a).t()
+    return xf @ _cpu32(w).t() + xa @ _cpu32(lora_b).t()
+
+
 def _bf16(t: torch.Tensor) -> torch.Tensor:
     return t.to(torch.bfloat16).to(torch.float32)
 

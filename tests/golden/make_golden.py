@@ -36,6 +36,7 @@ SOURCES = {
     "skinny_gemm": ("demo/skinny_gemm_test.py", "def", "gemm"),
     "dattn1_check": ("demo/dec_attn_second_part.py", "def", "torch_fn"),
     "rmsnorm_linear": ("python/cutedsl_kernels/rmsnorm_linear/attempt1/gemm.py", "assign", ("norm_a", "ref")),
+    "lora": ("python/cutedsl_kernels/lora/attempt1/gemm.py", "def", "torch_lora"),
 }
 
 
@@ -169,6 +170,19 @@ def make_gemms(ref: Path, gen):
                HERE / "dattn1.pt")
 
 
+def make_lora(ref: Path, gen):
+    # LoRA GEMM: gemm.py torch_lora() = (a @ b.t()) + (a @ lA.t() @ lB.t()) over globals a, b, lA, lB
+    m, n, k, r = 5, 160, 256, 16
+    a = _bf16_randn(gen, m, k)
+    b = _bf16_randn(gen, n, k, std=math.sqrt(2 / k))
+    lA = _bf16_randn(gen, r, k, std=math.sqrt(2 / k))
+    lB = _bf16_randn(gen, n, r, std=math.sqrt(2 / k))
+    ns = load_reference_code(ref, "lora", _ns(a=a.double(), b=b.double(), lA=lA.double(), lB=lB.double()))
+    y = ns["torch_lora"]()
+    torch.save({"x": a, "w": b, "lora_a": lA, "lora_b": lB, "y": y.float(), "source": SOURCES["lora"][0]},
+               HERE / "lora.pt")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--ref", default=os.environ.get("FK_REFERENCE_DIR", "/root/reference"))
@@ -181,6 +195,7 @@ def main():
     make_attention(ref, gen, B=2, Hq=8, Hkv=1, Lmax=200, lens=[200, 65], name="attn_gqa8")
     make_attention(ref, gen, B=3, Hq=4, Hkv=4, Lmax=96, lens=[96, 64, 63], name="attn_mha")
     make_gemms(ref, gen)
+    make_lora(ref, gen)
     for p in sorted(HERE.glob("*.pt")):
         print(f"{p.name}: {p.stat().st_size} bytes")
 

@@ -5,12 +5,14 @@ import torch
 import oracle
 from fused_kernels_cutedsl_lib_b200 import (
     Gemm4SM90,
+    LoraGemmSM90,
     RMSNormLinear1SM90,
     Swiglu2SM90,
     _native,
     alloc_workspace,
     compile_cutedsl,
     linear,
+    lora_linear,
     rmsnorm_linear,
     skinny_gemm,
     swiglu_gemm,
@@ -226,3 +228,59 @@ def test_tvm_ffi_entry_points_match_ctypes():
     mod.swiglu_gemm(x, wgu, y2, ws)
     torch.cuda.synchronize()
     assert torch.equal(y2, swiglu_gemm(x, wgu))
+    xa = mk(16, 16, 16, seed=10)[0]
+    lb = mk(16, 4096, 16, seed=11)[1]
+    mod.lora_gemm(x, w, xa, lb, y, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(y, lora_linear(x, w, lb, lora_xa=xa))
+
+
+# ---- LoRA: y = x W^T + (x A^T) B^T, the reference's lora/attempt1 GemmSM90 ----
+
+def test_lora_golden(golden):
+    g = golden("lora")
+    x, w, la, lb = (g[k].cuda() for k in ("x", "w", "lora_a", "lora_b"))
+    y = lora_linear(x, w, lb, lora_a=la)
+    finish()
+    assert_close(y, g["y"])
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 64, 200, 300])
+@pytest.mark.parametrize("rank", [16, 64, 72])
+def test_lora_matches_oracle(M, rank):
+    N, K = 1536, 1024
+    x, w = mk(M, N, K, seed=M + rank)
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    la = (0.03 * torch.randn(rank, K, generator=g, device="cuda")).bfloat16()
+    lb = (0.03 * torch.randn(N, rank, generator=g, device="cuda")).bfloat16()
+    res = torch.randn(M, N, generator=g, device="cuda").bfloat16()
+    xa = linear(x, la)
+    y = lora_linear(x, w, lb, lora_xa=xa, residual=res)
+    finish()
+    assert_close(y, oracle.lora_linear(x, w, None, lb, lora_xa=xa) + res.float().cpu())
+    # the rank-r term matters: without it the check fails
+    base = oracle.linear(x, w) + res.float().cpu()
+    assert ((y.float().cpu() - base).abs().max() > 0.05)
+
+
+def test_lora_kernel_object_reference_call_shape():
+    M, N, K, r = 32, 512, 256, 16
+    x, w = mk(M, N, K, seed=4)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    la = (0.05 * torch.randn(r, K, generator=g, device="cuda")).bfloat16()
+    lb = (0.05 * torch.randn(N, r, generator=g, device="cuda")).bfloat16()
+    xa = (x.float() @ la.float().t()).bfloat16()  # the reference computes lora_xA with torch before the call
+    c = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    LoraGemmSM90(tile_shape_mn=(128, 256), lora_dim=r)(x, w, xa, lb, c)
+    finish()
+    assert_close(c, oracle.lora_linear(x, w, None, lb, lora_xa=xa))
+
+
+def test_lora_argument_errors():
+    x, w = mk(4, 256, 128)
+    lb = torch.zeros(256, 12, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        lora_linear(x, w, lb, lora_a=torch.zeros(12, 128, dtype=torch.bfloat16, device="cuda"))  # rank 12
+    lb = torch.zeros(256, 16, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        lora_linear(x, w, lb)  # neither lora_a nor lora_xa

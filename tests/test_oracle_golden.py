@@ -38,6 +38,8 @@ def test_gemm_goldens(golden):
     _close(oracle.swiglu_separate(g["x"], g["b"], g["b1"]), g["y"])
     g = golden("dattn1")
     _close(oracle.dattn1_reference(g["Q"], g["K"], g["V"]), g["O"])
+    g = golden("lora")
+    _close(oracle.lora_linear(g["x"], g["w"], g["lora_a"], g["lora_b"]), g["y"])
 
 
 def test_swiglu_forms_agree(golden):
