@@ -20,6 +20,7 @@ from .gemm import (
     swiglu_gemm2,
     workspace_bytes,
 )
+from .prefill_attention import FlashSM90, flash_attention
 from .decoding_attention import (
     DAttn1,
     DAttn2,
@@ -48,6 +49,8 @@ __all__ = [
     "swiglu_gemm",
     "swiglu_gemm2",
     "workspace_bytes",
+    "FlashSM90",
+    "flash_attention",
     "DAttn1",
     "DAttn2",
     "DecodeAttention",

@@ -58,6 +58,10 @@ SIGNATURES: dict[str, tuple] = {
         [_p, ctypes.c_longlong, _c_int, _c_int, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p],
     ),
     "fk_dattn1": (_c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
+    "fk_prefill_attn_fwd": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _p],
+    ),
     "fk_lora_linear": (
         _c_int,
         [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p],

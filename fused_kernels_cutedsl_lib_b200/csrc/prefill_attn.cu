@@ -1,0 +1,464 @@
+// Prefill (full-sequence) attention on sm_100a tensor cores:
+//   O[b, h] = softmax(Q[b, h] K[b, hk]^T * scale) V[b, hk],  hk = h / (H / Hkv)
+// for Q [B, H, Lq, D], K/V [B, Hkv, Lkv, D], O [B, H, Lq, D] bf16 (D = 64 or
+// 128), non-causal, with an optional natural-log LSE [B, H, Lq] fp32.
+//
+// Replaces the reference's FlashSM90 (python/cutedsl_kernels/attn/
+// attempt6_epi_pipeline/attn.py:73-241: wgmma S = Q K^T, exp2-domain online
+// softmax in registers (my_softmax.py:35-105), O += P V, checked against
+// F.scaled_dot_product_attention in tests.py:85 and attn_reimpl attn.py:778-784).
+//
+// One CTA per (128-query tile, b*h), 192 threads:
+//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
+//               into two rings (3-D tensor maps: keys past Lkv read as zero)
+//   warp 1      allocates TMEM (S0 | S1 | O); one lane issues tcgen05.mma:
+//               S_j = Q K_j^T into TMEM buffer j&1 (both operands K-major),
+//               then O += P_j V_j (P K-major from shared memory, V MN-major
+//               straight from the TMA tile), committing to mbarriers
+//   warps 2-5   softmax: thread = query row = TMEM lane. tcgen05.ld S_j,
+//               mask keys past Lkv, exp2-domain running max; the O rescale
+//               (tcgen05.ld/st of the row) runs only when a warp's max grows
+//               by more than 2^8, otherwise P keeps the stale max, which the
+//               final 1/l normalisation cancels exactly. P_j is rounded to
+//               bf16 into a 128B-swizzled tile for the next MMA. Epilogue:
+//               O / l to bf16, LSE = (m + log2 l) ln 2.
+// Every mbarrier wait is bounded (device error word + orderly exit).
+#include <math.h>
+
+#include "common.cuh"
+#include "fk_b200.h"
+
+namespace fk {
+namespace fa {
+
+constexpr int BM = 128;  // queries per tile (UMMA M, TMEM lanes)
+constexpr int BN = 128;  // keys per tile
+constexpr int NTHREADS = 192;
+constexpr int ATOM = 128 * 128;  // one 128-row x 64-element bf16 swizzle block: 16 KB
+constexpr int P_BYTES = 2 * ATOM;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr size_t kSmemLimit = 227 * 1024;
+
+template <int D>
+struct Cfg {
+  static constexpr int TILE = D * 256;  // 128 rows x D x 2 B
+  static constexpr int KS = D == 64 ? 3 : 2;
+  static constexpr int VS = D == 64 ? 3 : 2;
+  static constexpr int NP = 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + TILE;
+  static constexpr int V_OFF = K_OFF + KS * TILE;
+  static constexpr int P_OFF = V_OFF + VS * TILE;
+  static constexpr int BAR_OFF = P_OFF + NP * P_BYTES;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 4 + 2 * NP + 1;
+  static constexpr size_t SMEM = 1024 + BAR_OFF + NBAR * 8 + 16;
+  static_assert(SMEM <= kSmemLimit, "shared memory budget");
+};
+
+struct Params {
+  __nv_bfloat16* o;
+  float* lse;
+  int* err;
+  int H, G, Lq, Lkv, nkv;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand, 128B swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// MN-major operand, 128B swizzle: 64-element MN chunks `lbo` bytes apart,
+// 8-row K groups 1024 B apart.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// kind::f16, A = B = bf16, D = f32, M = 128, N = n; b_mn selects an MN-major B.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane (no wait).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x on the special-function unit (PTX ex2.approx; flushes subnormal results).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, Params p) {
+  using C = Cfg<D>;
+  constexpr int KS = C::KS, VS = C::VS, NP = C::NP;
+  constexpr int NA = D / 64;  // 64-element swizzle atoms along D
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;   // [2]
+  uint64_t* s_empty = s_full + 2;    // [2]
+  uint64_t* p_full = s_empty + 2;    // [NP]
+  uint64_t* p_empty = p_full + NP;   // [NP]: also "O holds P_j V_j" for the j that used the buffer
+  uint64_t* done = p_empty + NP;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, bh = blockIdx.y;
+  const int kv_bh = (bh / p.H) * (p.H / p.G) + (bh % p.H) / p.G;
+  const int n = p.nkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    for (int i = 0; i < NP; ++i) {
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(done, 4);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const uint64_t pol_q = l2_policy_evict_first();
+      const uint64_t pol_kv = l2_policy_evict_last();  // re-read by every query tile of the head
+      mbar_arrive_expect_tx(q_full, C::TILE);
+#pragma unroll
+      for (int a = 0; a < NA; ++a) tma_load_3d(smem + C::Q_OFF + a * ATOM, &tmQ, q_full, a * 64, qt * BM, bh, pol_q);
+      for (int j = 0; j < n; ++j) {
+        const int ks = j % KS, vs = j % VS;
+        if (!mbar_wait(&k_empty[ks], ((j / KS) & 1) ^ 1, p.err, kDevErrEmptyWait)) break;
+        mbar_arrive_expect_tx(&k_full[ks], C::TILE);
+#pragma unroll
+        for (int a = 0; a < NA; ++a)
+          tma_load_3d(smem + C::K_OFF + ks * C::TILE + a * ATOM, &tmK, &k_full[ks], a * 64, j * BN, kv_bh, pol_kv);
+        if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, p.err, kDevErrEmptyWait)) break;
+        mbar_arrive_expect_tx(&v_full[vs], C::TILE);
+#pragma unroll
+        for (int a = 0; a < NA; ++a)
+          tma_load_3d(smem + C::V_OFF + vs * C::TILE + a * ATOM, &tmV, &v_full[vs], a * 64, j * BN, kv_bh, pol_kv);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+
+  if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    bool ok = true;
+    if (lane == 0) {
+      constexpr uint32_t IDS = idesc_bf16(BN, false);
+      constexpr uint32_t IDO = idesc_bf16(D, true);
+      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
+      auto issue_s = [&](int j) -> bool {
+        const int ks = j % KS, sb = j & 1;
+        if (!mbar_wait(&k_full[ks], (j / KS) & 1, p.err, kDevErrFullWait)) return false;
+        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, p.err, kDevErrMmaWait)) return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + C::K_OFF + ks * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
+          umma(tmem + sb * BN, desc_k_sw128(q_base + off), desc_k_sw128(k_base + off), IDS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&k_empty[ks]);
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int pb = j % NP, vs = j % VS;
+        if (!mbar_wait(&p_full[pb], (j / NP) & 1, p.err, kDevErrMmaWait)) return false;
+        if (!mbar_wait(&v_full[vs], (j / VS) & 1, p.err, kDevErrFullWait)) return false;
+        tc_fence_after();
+        const uint32_t p_base = smem_u32(smem + C::P_OFF + pb * P_BYTES);
+        const uint32_t v_base = smem_u32(smem + C::V_OFF + vs * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t da = desc_k_sw128(p_base + (kk >> 2) * ATOM + (kk & 3) * 32);
+          const uint64_t db = desc_mn_sw128(v_base + kk * 2048, ATOM);
+          umma(tmem + 2 * BN, da, db, IDO, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&v_empty[vs]);
+        umma_commit(&p_empty[pb]);
+        return true;
+      };
+      if (!mbar_wait(q_full, 0, p.err, kDevErrFullWait)) ok = false;
+      if (ok && n > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n && !issue_s(j + 1)) ok = false;
+        if (ok && !issue_pv(j)) ok = false;
+      }
+    }
+    __syncwarp();
+    // TMEM is freed only after the softmax warps have read O.
+    mbar_wait(done, 0, p.err, kDevErrMmaWait);
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+    return;
+  }
+
+  // --------------------------------- softmax ---------------------------------
+  const int quarter = warp & 3;
+  const int row = 32 * quarter + lane;
+  const uint32_t tlane = tmem + ((uint32_t)(32 * quarter) << 16);
+  uint8_t* prow = smem + C::P_OFF + row * 128;
+  const int sw = row & 7;
+  float m_used = -INFINITY, l = 0.f;
+  float s[BN];
+  bool ok = true;
+  for (int j = 0; j < n; ++j) {
+    const int sb = j & 1;
+    if (!mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, kDevErrMmaWait)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) tmem_ld32(tlane + sb * BN + c * 32, s + c * 32);
+    tmem_ld_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s_empty[sb]);
+
+    const int valid = p.Lkv - j * BN;  // keys of this tile inside the sequence
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < BN; ++i) {
+      s[i] = (i < valid) ? s[i] * p.scale_log2 : -INFINITY;
+      mx = fmaxf(mx, s[i]);
+    }
+    // Rescale O only when some row's max grew past the threshold (warp-uniform:
+    // tcgen05.ld/st are warp-collective). Rows whose max did not move get alpha = 1.
+    const bool grow = mx > m_used + kRescaleThreshold;
+    if (__any_sync(0xffffffffu, grow)) {
+      const float m_new = fmaxf(m_used, mx);
+      const float alpha = ex2(m_used - m_new);  // 0 on the first tile (m_used = -inf)
+      l *= alpha;
+      m_used = m_new;
+      if (j > 0) {
+        const int pj = (j - 1) % NP;
+        if (!mbar_wait(&p_empty[pj], ((j - 1) / NP) & 1, p.err, kDevErrMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float o[32];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(tlane + 2 * BN + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tlane + 2 * BN + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+    }
+    float rs = 0.f;
+#pragma unroll
+    for (int i = 0; i < BN; ++i) {
+      s[i] = ex2(s[i] - m_used);
+      rs += s[i];
+    }
+    l += rs;
+    // P_j into buffer j % NP once P_{j-NP} V has been consumed.
+    const int pb = j % NP;
+    if (j >= NP && !mbar_wait(&p_empty[pb], ((j / NP) - 1) & 1, p.err, kDevErrMmaWait)) {
+      ok = false;
+      break;
+    }
+    uint8_t* pr = prow + pb * P_BYTES;
+#pragma unroll
+    for (int c = 0; c < BN / 8; ++c) {
+      uint4 v;
+      v.x = pack_bf16x2(s[8 * c + 0], s[8 * c + 1]);
+      v.y = pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
+      v.z = pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
+      v.w = pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
+      *reinterpret_cast<uint4*>(pr + (c >> 3) * ATOM + (((c & 7) ^ sw) << 4)) = v;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p_full[pb]);
+  }
+
+  // ------------------------------ epilogue ------------------------------
+  const int qrow = qt * BM + row;
+  if (ok && n > 0 && mbar_wait(&p_empty[(n - 1) % NP], ((n - 1) / NP) & 1, p.err, kDevErrMmaWait)) {
+    tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = p.o + ((size_t)bh * p.Lq + qrow) * D;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      float o[32];
+      tmem_ld32(tlane + 2 * BN + c * 32, o);
+      tmem_ld_wait();
+      if (qrow < p.Lq) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 v;
+          v.x = pack_bf16x2(o[i + 0] * inv, o[i + 1] * inv);
+          v.y = pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv);
+          v.z = pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv);
+          v.w = pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
+        }
+      }
+    }
+    if (p.lse && qrow < p.Lq)
+      p.lse[(size_t)bh * p.Lq + qrow] = l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(done);
+}
+
+template <int D>
+static int launch(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int Hkv, int Lq,
+                  int Lkv, float scale, cudaStream_t stream) {
+  using Cf = Cfg<D>;
+  int* err = device_error_word();
+  if (!err) return fail(kErrCuda, "device error word unavailable");
+  CUtensorMap tmQ, tmK, tmV;
+  const uint32_t box[3] = {64, 128, 1};
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)Lq, (uint64_t)B * H};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)Lq * D * 2};
+    int rc = encode_tma(&tmQ, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)Lkv, (uint64_t)B * Hkv};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)Lkv * D * 2};
+    int rc = encode_tma(&tmK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(k), dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = encode_tma(&tmV, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(v), dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  Params p;
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.lse = lse;
+  p.err = err;
+  p.H = H;
+  p.G = H / Hkv;
+  p.Lq = Lq;
+  p.Lkv = Lkv;
+  p.nkv = (Lkv + BN - 1) / BN;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  auto kern = fmha_fwd_kernel<D>;
+  FK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
+  const dim3 grid((unsigned)((Lq + BM - 1) / BM), (unsigned)(B * H), 1);
+  kern<<<grid, NTHREADS, Cf::SMEM, stream>>>(tmQ, tmK, tmV, p);
+  FK_CHECK_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+}  // namespace fa
+}  // namespace fk
+
+using namespace fk;
+
+extern "C" int fk_prefill_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
+                                   int num_heads_q, int num_heads_kv, int seqlen_q, int seqlen_kv, int head_dim,
+                                   float softmax_scale, void* stream) {
+  FK_CHECK_ARG(q && k && v && out, "null tensor pointer");
+  FK_CHECK_ARG(batch >= 1 && seqlen_q >= 1 && seqlen_kv >= 1, "sizes must be positive");
+  FK_CHECK_ARG(num_heads_kv >= 1 && num_heads_q >= num_heads_kv && num_heads_q % num_heads_kv == 0,
+               "num_heads_q must be a positive multiple of num_heads_kv");
+  FK_CHECK_ARG(head_dim == 64 || head_dim == 128, "head_dim must be 64 or 128");
+  FK_CHECK_ARG((long long)batch * num_heads_q <= 65535, "batch * num_heads_q must be <= 65535");
+  FK_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 && ((uintptr_t)v & 15) == 0 &&
+                   ((uintptr_t)out & 15) == 0,
+               "tensors must be 16-byte aligned");
+  FK_CHECK_ARG(softmax_scale > 0.f, "softmax_scale must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    return fa::launch<64>(q, k, v, out, lse, batch, num_heads_q, num_heads_kv, seqlen_q, seqlen_kv, softmax_scale,
+                          st);
+  return fa::launch<128>(q, k, v, out, lse, batch, num_heads_q, num_heads_kv, seqlen_q, seqlen_kv, softmax_scale,
+                         st);
+}

@@ -220,6 +220,18 @@ FK_API int fk_rmsnorm_swiglu(const void* x, const void* gamma, const void* w_gat
                              int M, int N, int K, float eps, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Prefill attention O = softmax(Q K^T * softmax_scale) V on the tensor cores:
+ * q / out [batch, num_heads_q, seqlen_q, head_dim], k / v [batch, num_heads_kv,
+ * seqlen_kv, head_dim] bf16 contiguous (q head h reads kv head
+ * h / (num_heads_q / num_heads_kv)), head_dim 64 or 128, no mask. lse (may be
+ * null) [batch, num_heads_q, seqlen_q] fp32 natural-log logsumexp of the
+ * scaled scores. Replaces FlashSM90(...)(mQ, mK, mV, mO, softmax_scale, stream)
+ * of python/cutedsl_kernels/attn/attempt6_epi_pipeline/attn.py:73-175
+ * (checked against F.scaled_dot_product_attention, tests.py:85). */
+FK_API int fk_prefill_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int batch,
+                               int num_heads_q, int num_heads_kv, int seqlen_q, int seqlen_kv, int head_dim,
+                               float softmax_scale, void* stream);
+
 /* LoRA linear: y[M, N] = x W^T + xA B^T (+ residual when non-null), with
  * xA = x A^T given as [M, rank] and B as [N, rank] (rank a multiple of 8).
  * Replaces GemmSM90(...)(a, b, lora_xA, lora_B, c, stream) of

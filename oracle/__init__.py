@@ -18,6 +18,7 @@ from .ops import (
     decode_layer,
     linear,
     lora_linear,
+    prefill_attention,
     rmsnorm,
     rmsnorm_linear,
     silu,
@@ -30,6 +31,7 @@ __all__ = [
     "decode_attention",
     "decode_layer",
     "lora_linear",
+    "prefill_attention",
     "linear",
     "rmsnorm",
     "rmsnorm_linear",

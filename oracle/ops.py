@@ -54,6 +54,26 @@ def decode_attention(q, k_cache, v_cache, cache_seqlens, softmax_scale=None):
     return out, lse
 
 
+def prefill_attention(q, k, v, softmax_scale=None):
+    """Full-sequence attention in fp32, the reference's ``attn_reimpl``
+    (attn/attempt6_epi_pipeline/attn.py:778-784: ``p = q k^T * scale * log2 e``,
+    ``exp2(p - rowmax)``, ``(p v) / rowsum``), with grouped kv heads
+    (q head h reads kv head h // (Hq // Hkv)). Returns (out, lse) with the
+    natural-log logsumexp of the scaled scores. q [B, Hq, Lq, D], k/v [B, Hkv, Lkv, D].
+    """
+    qf, kf, vf = _cpu32(q), _cpu32(k), _cpu32(v)
+    B, Hq, Lq, D = qf.shape
+    g = Hq // kf.shape[1]
+    kf = kf.repeat_interleave(g, dim=1)
+    vf = vf.repeat_interleave(g, dim=1)
+    scale = D ** -0.5 if softmax_scale is None else float(softmax_scale)
+    s = (qf @ kf.transpose(2, 3)) * scale
+    lse = torch.logsumexp(s, dim=-1)
+    p = torch.exp2((s - s.amax(dim=-1, keepdim=True)) * math.log2(math.e))
+    out = (p @ vf) / p.sum(dim=-1, keepdim=True)
+    return out, lse
+
+
 def dattn1_reference(Q, K, V):
     """The reference decode kernel's own check: ``(Q @ K^T) @ Vt`` with V given transposed.
 

@@ -183,6 +183,19 @@ def make_lora(ref: Path, gen):
                HERE / "lora.pt")
 
 
+def make_prefill(ref: Path, gen, B, H, Lq, Lkv, D, name):
+    # Full-sequence attention: attn_reimpl(q, k, v) of attn/attempt6_epi_pipeline/attn.py on
+    # [b, h, seqlen, d] inputs drawn like that kernel's tests (tests.py generate_input: randn + 0.5).
+    q = (torch.randn(B, H, Lq, D, generator=gen, dtype=torch.float64) + 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, H, Lkv, D, generator=gen, dtype=torch.float64) + 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, H, Lkv, D, generator=gen, dtype=torch.float64) + 0.5).to(torch.bfloat16)
+    ns = load_reference_code(ref, "attn_reimpl", _ns())
+    out = ns["attn_reimpl"](q.double(), k.double(), v.double())
+    lse = torch.logsumexp((q.double() @ k.double().transpose(2, 3)) * D ** -0.5, dim=-1)
+    torch.save({"q": q, "k": k, "v": v, "out": out.float(), "lse": lse.float(),
+                "source": SOURCES["attn_reimpl"][0]}, HERE / f"{name}.pt")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--ref", default=os.environ.get("FK_REFERENCE_DIR", "/root/reference"))
@@ -196,6 +209,8 @@ def main():
     make_attention(ref, gen, B=3, Hq=4, Hkv=4, Lmax=96, lens=[96, 64, 63], name="attn_mha")
     make_gemms(ref, gen)
     make_lora(ref, gen)
+    make_prefill(ref, gen, B=1, H=2, Lq=130, Lkv=200, D=64, name="prefill_d64")
+    make_prefill(ref, gen, B=1, H=2, Lq=64, Lkv=136, D=128, name="prefill_d128")
     for p in sorted(HERE.glob("*.pt")):
         print(f"{p.name}: {p.stat().st_size} bytes")
 

@@ -27,6 +27,14 @@ def test_empty_row_is_zero_and_neg_inf(golden):
     assert torch.all(out[3] == 0) and torch.all(torch.isneginf(lse[3]))
 
 
+def test_prefill_goldens(golden):
+    for name in ("prefill_d64", "prefill_d128"):
+        g = golden(name)
+        out, lse = oracle.prefill_attention(g["q"], g["k"], g["v"])
+        _close(out, g["out"])
+        _close(lse, g["lse"])
+
+
 def test_gemm_goldens(golden):
     g = golden("skinny_gemm")
     _close(oracle.linear(g["x"], g["w"]), g["y"])
