@@ -8,20 +8,23 @@
 // softmax in registers (my_softmax.py:35-105), O += P V, checked against
 // F.scaled_dot_product_attention in tests.py:85 and attn_reimpl attn.py:778-784).
 //
-// One CTA per (128-query tile, b*h), 192 threads:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 keys
-//               into two rings (3-D tensor maps: keys past Lkv read as zero)
-//   warp 1      allocates TMEM (S0 | S1 | O); one lane issues tcgen05.mma:
-//               S_j = Q K_j^T into TMEM buffer j&1 (both operands K-major),
-//               then O += P_j V_j (P K-major from shared memory, V MN-major
+// One CTA per (256 queries = two 128-row tiles A and B, b*h), 320 threads:
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: thread = query
+//               row = TMEM lane (warp w reads lanes 32*(w%4)..). Two softmax
+//               warps per SM sub-partition hide each other's latency.
+//               tcgen05.ld S_t(j), mask keys past Lkv, exp2-domain running max;
+//               the O rescale (tcgen05.ld/st of the row) runs only when a
+//               warp's max grows by more than 2^8, otherwise P keeps the stale
+//               max, which the final 1/l normalisation cancels exactly. P_t(j)
+//               is rounded to bf16 into a 128B-swizzled tile for the next MMA.
+//               Epilogue: O / l to bf16, LSE = (m + log2 l) ln 2.
+//   warp 8      TMA producer: both Q tiles once, then K_0, V_0, K_1, V_1, ...
+//               (128 keys each) through one ring shared by the two tiles
+//               (3-D tensor maps: keys past Lkv read as zero)
+//   warp 9      allocates TMEM (S_A | S_B | O_A | O_B); one lane issues
+//               tcgen05.mma: S_t(j) = Q_t K_j^T (both operands K-major), then
+//               O_t += P_t(j) V_j (P K-major from shared memory, V MN-major
 //               straight from the TMA tile), committing to mbarriers
-//   warps 2-5   softmax: thread = query row = TMEM lane. tcgen05.ld S_j,
-//               mask keys past Lkv, exp2-domain running max; the O rescale
-//               (tcgen05.ld/st of the row) runs only when a warp's max grows
-//               by more than 2^8, otherwise P keeps the stale max, which the
-//               final 1/l normalisation cancels exactly. P_j is rounded to
-//               bf16 into a 128B-swizzled tile for the next MMA. Epilogue:
-//               O / l to bf16, LSE = (m + log2 l) ln 2.
 // Every mbarrier wait is bounded (device error word + orderly exit).
 #include <math.h>
 
@@ -32,8 +35,10 @@ namespace fk {
 namespace fa {
 
 constexpr int BM = 128;  // queries per tile (UMMA M, TMEM lanes)
+constexpr int NT = 2;    // query tiles per CTA
 constexpr int BN = 128;  // keys per tile
-constexpr int NTHREADS = 192;
+constexpr int NTHREADS = 320;
+constexpr int TMA_WARP = 8, MMA_WARP = 9;
 constexpr int ATOM = 128 * 128;  // one 128-row x 64-element bf16 swizzle block: 16 KB
 constexpr int P_BYTES = 2 * ATOM;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -42,17 +47,15 @@ constexpr size_t kSmemLimit = 227 * 1024;
 template <int D>
 struct Cfg {
   static constexpr int TILE = D * 256;  // 128 rows x D x 2 B
-  static constexpr int KS = D == 64 ? 3 : 2;
-  static constexpr int VS = D == 64 ? 3 : 2;
-  static constexpr int NP = 2;
+  static constexpr int NS = D == 64 ? 6 : 3;  // K/V ring stages
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + TILE;
-  static constexpr int V_OFF = K_OFF + KS * TILE;
-  static constexpr int P_OFF = V_OFF + VS * TILE;
-  static constexpr int BAR_OFF = P_OFF + NP * P_BYTES;
-  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 4 + 2 * NP + 1;
+  static constexpr int KV_OFF = Q_OFF + NT * TILE;
+  static constexpr int P_OFF = KV_OFF + NS * TILE;
+  static constexpr int BAR_OFF = P_OFF + NT * P_BYTES;
+  static constexpr int NBAR = 1 + 2 * NS + 4 * NT + 1;
   static constexpr size_t SMEM = 1024 + BAR_OFF + NBAR * 8 + 16;
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
+  static constexpr int O_COL = NT * BN;  // O_t at column O_COL + t * D
 };
 
 struct Params {
@@ -142,21 +145,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, Params p) {
   using C = Cfg<D>;
-  constexpr int KS = C::KS, VS = C::VS, NP = C::NP;
+  constexpr int NS = C::NS;
   constexpr int NA = D / 64;  // 64-element swizzle atoms along D
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + KS;
-  uint64_t* v_full = k_empty + KS;
-  uint64_t* v_empty = v_full + VS;
-  uint64_t* s_full = v_empty + VS;   // [2]
-  uint64_t* s_empty = s_full + 2;    // [2]
-  uint64_t* p_full = s_empty + 2;    // [NP]
-  uint64_t* p_empty = p_full + NP;   // [NP]: also "O holds P_j V_j" for the j that used the buffer
-  uint64_t* done = p_empty + NP;
+  uint64_t* kv_full = q_full + 1;    // [NS]
+  uint64_t* kv_empty = kv_full + NS; // [NS]
+  uint64_t* s_full = kv_empty + NS;  // [NT]
+  uint64_t* s_empty = s_full + NT;   // [NT]
+  uint64_t* p_full = s_empty + NT;   // [NT]
+  uint64_t* p_empty = p_full + NT;   // [NT]: also "O_t holds P_t(j) V_j"
+  uint64_t* done = p_empty + NT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -166,26 +167,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < KS; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < VS; ++i) {
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&p_empty[t], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-    }
-    for (int i = 0; i < NP; ++i) {
-      mbar_init(&p_full[i], 4);
-      mbar_init(&p_empty[i], 1);
-    }
-    mbar_init(done, 4);
+    mbar_init(done, 8);
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
@@ -194,72 +189,79 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == TMA_WARP) {
     // ------------------------------ TMA producer ------------------------------
+    // Ring items: K_j = item 2j, V_j = item 2j + 1, stage = item % NS.
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();  // re-read by every query tile of the head
-      mbar_arrive_expect_tx(q_full, C::TILE);
+      mbar_arrive_expect_tx(q_full, NT * C::TILE);
 #pragma unroll
-      for (int a = 0; a < NA; ++a) tma_load_3d(smem + C::Q_OFF + a * ATOM, &tmQ, q_full, a * 64, qt * BM, bh, pol_q);
-      for (int j = 0; j < n; ++j) {
-        const int ks = j % KS, vs = j % VS;
-        if (!mbar_wait(&k_empty[ks], ((j / KS) & 1) ^ 1, p.err, kDevErrEmptyWait)) break;
-        mbar_arrive_expect_tx(&k_full[ks], C::TILE);
+      for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int a = 0; a < NA; ++a)
-          tma_load_3d(smem + C::K_OFF + ks * C::TILE + a * ATOM, &tmK, &k_full[ks], a * 64, j * BN, kv_bh, pol_kv);
-        if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, p.err, kDevErrEmptyWait)) break;
-        mbar_arrive_expect_tx(&v_full[vs], C::TILE);
+          tma_load_3d(smem + C::Q_OFF + t * C::TILE + a * ATOM, &tmQ, q_full, a * 64, (qt * NT + t) * BM, bh, pol_q);
+      for (int it = 0; it < 2 * n; ++it) {
+        const int st = it % NS;
+        if (!mbar_wait(&kv_empty[st], ((it / NS) & 1) ^ 1, p.err, kDevErrEmptyWait)) break;
+        mbar_arrive_expect_tx(&kv_full[st], C::TILE);
+        const CUtensorMap* map = (it & 1) ? &tmV : &tmK;
 #pragma unroll
         for (int a = 0; a < NA; ++a)
-          tma_load_3d(smem + C::V_OFF + vs * C::TILE + a * ATOM, &tmV, &v_full[vs], a * 64, j * BN, kv_bh, pol_kv);
+          tma_load_3d(smem + C::KV_OFF + st * C::TILE + a * ATOM, map, &kv_full[st], a * 64, (it >> 1) * BN, kv_bh,
+                      pol_kv);
       }
     }
     __syncwarp();
     return;
   }
 
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     // ------------------------------ MMA issuer ------------------------------
     bool ok = true;
     if (lane == 0) {
       constexpr uint32_t IDS = idesc_bf16(BN, false);
       constexpr uint32_t IDO = idesc_bf16(D, true);
-      const uint32_t q_base = smem_u32(smem + C::Q_OFF);
+      // S_A(j), S_B(j) from K_j (ring item 2j); K_j's stage is freed after S_B(j).
       auto issue_s = [&](int j) -> bool {
-        const int ks = j % KS, sb = j & 1;
-        if (!mbar_wait(&k_full[ks], (j / KS) & 1, p.err, kDevErrFullWait)) return false;
-        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, p.err, kDevErrMmaWait)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + C::K_OFF + ks * C::TILE);
+        const int it = 2 * j, st = it % NS;
+        if (!mbar_wait(&kv_full[st], (it / NS) & 1, p.err, kDevErrFullWait)) return false;
+        const uint32_t k_base = smem_u32(smem + C::KV_OFF + st * C::TILE);
+        for (int t = 0; t < NT; ++t) {
+          if (!mbar_wait(&s_empty[t], (j & 1) ^ 1, p.err, kDevErrMmaWait)) return false;
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(smem + C::Q_OFF + t * C::TILE);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
-          umma(tmem + sb * BN, desc_k_sw128(q_base + off), desc_k_sw128(k_base + off), IDS, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
+            umma(tmem + t * BN, desc_k_sw128(q_base + off), desc_k_sw128(k_base + off), IDS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
         }
-        umma_commit(&k_empty[ks]);
-        umma_commit(&s_full[sb]);
+        umma_commit(&kv_empty[st]);
         return true;
       };
+      // O_A += P_A(j) V_j, O_B += P_B(j) V_j (ring item 2j + 1, freed after both).
       auto issue_pv = [&](int j) -> bool {
-        const int pb = j % NP, vs = j % VS;
-        if (!mbar_wait(&p_full[pb], (j / NP) & 1, p.err, kDevErrMmaWait)) return false;
-        if (!mbar_wait(&v_full[vs], (j / VS) & 1, p.err, kDevErrFullWait)) return false;
-        tc_fence_after();
-        const uint32_t p_base = smem_u32(smem + C::P_OFF + pb * P_BYTES);
-        const uint32_t v_base = smem_u32(smem + C::V_OFF + vs * C::TILE);
+        const int it = 2 * j + 1, st = it % NS;
+        if (!mbar_wait(&kv_full[st], (it / NS) & 1, p.err, kDevErrFullWait)) return false;
+        const uint32_t v_base = smem_u32(smem + C::KV_OFF + st * C::TILE);
+        for (int t = 0; t < NT; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, p.err, kDevErrMmaWait)) return false;
+          tc_fence_after();
+          const uint32_t p_base = smem_u32(smem + C::P_OFF + t * P_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t da = desc_k_sw128(p_base + (kk >> 2) * ATOM + (kk & 3) * 32);
-          const uint64_t db = desc_mn_sw128(v_base + kk * 2048, ATOM);
-          umma(tmem + 2 * BN, da, db, IDO, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t da = desc_k_sw128(p_base + (kk >> 2) * ATOM + (kk & 3) * 32);
+            const uint64_t db = desc_mn_sw128(v_base + kk * 2048, ATOM);
+            umma(tmem + C::O_COL + t * D, da, db, IDO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&p_empty[t]);
         }
-        umma_commit(&v_empty[vs]);
-        umma_commit(&p_empty[pb]);
+        umma_commit(&kv_empty[st]);
         return true;
       };
       if (!mbar_wait(q_full, 0, p.err, kDevErrFullWait)) ok = false;
@@ -278,101 +280,110 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 
   // --------------------------------- softmax ---------------------------------
+  const int t = warp >> 2;  // query tile
   const int quarter = warp & 3;
   const int row = 32 * quarter + lane;
   const uint32_t tlane = tmem + ((uint32_t)(32 * quarter) << 16);
-  uint8_t* prow = smem + C::P_OFF + row * 128;
+  const uint32_t s_col = t * BN, o_col = C::O_COL + t * D;
+  uint8_t* prow = smem + C::P_OFF + t * P_BYTES + row * 128;
   const int sw = row & 7;
   float m_used = -INFINITY, l = 0.f;
   float s[BN];
   bool ok = true;
   for (int j = 0; j < n; ++j) {
-    const int sb = j & 1;
-    if (!mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, kDevErrMmaWait)) {
+    if (!mbar_wait(&s_full[t], j & 1, p.err, kDevErrMmaWait)) {
       ok = false;
       break;
     }
     tc_fence_after();
 #pragma unroll
-    for (int c = 0; c < BN / 32; ++c) tmem_ld32(tlane + sb * BN + c * 32, s + c * 32);
+    for (int c = 0; c < BN / 32; ++c) tmem_ld32(tlane + s_col + c * 32, s + c * 32);
     tmem_ld_wait();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&s_empty[sb]);
+    if (lane == 0) mbar_arrive(&s_empty[t]);
 
     const int valid = p.Lkv - j * BN;  // keys of this tile inside the sequence
-    float mx = -INFINITY;
+    if (valid < BN) {                  // tail tile only (warp-uniform)
 #pragma unroll
-    for (int i = 0; i < BN; ++i) {
-      s[i] = (i < valid) ? s[i] * p.scale_log2 : -INFINITY;
-      mx = fmaxf(mx, s[i]);
+      for (int i = 0; i < BN; ++i)
+        if (i >= valid) s[i] = -INFINITY;
     }
-    // Rescale O only when some row's max grew past the threshold (warp-uniform:
-    // tcgen05.ld/st are warp-collective). Rows whose max did not move get alpha = 1.
-    const bool grow = mx > m_used + kRescaleThreshold;
-    if (__any_sync(0xffffffffu, grow)) {
-      const float m_new = fmaxf(m_used, mx);
-      const float alpha = ex2(m_used - m_new);  // 0 on the first tile (m_used = -inf)
-      l *= alpha;
-      m_used = m_new;
-      if (j > 0) {
-        const int pj = (j - 1) % NP;
-        if (!mbar_wait(&p_empty[pj], ((j - 1) / NP) & 1, p.err, kDevErrMmaWait)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float o[32];
+    // Row max of the raw scores (scale > 0), as a tree: 4 independent chains.
+    float mx4[4];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(tlane + 2 * BN + c * 32, o);
-          tmem_ld_wait();
+    for (int u = 0; u < 4; ++u) mx4[u] = s[u];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tlane + 2 * BN + c * 32, o);
-        }
-        tmem_st_wait();
-      }
-    }
-    float rs = 0.f;
+    for (int i = 4; i < BN; i += 4)
 #pragma unroll
-    for (int i = 0; i < BN; ++i) {
-      s[i] = ex2(s[i] - m_used);
-      rs += s[i];
-    }
-    l += rs;
-    // P_j into buffer j % NP once P_{j-NP} V has been consumed.
-    const int pb = j % NP;
-    if (j >= NP && !mbar_wait(&p_empty[pb], ((j / NP) - 1) & 1, p.err, kDevErrMmaWait)) {
+      for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], s[i + u]);
+    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+    // P_t(j-1) V_{j-1} must be complete before O_t is rescaled or P_t is rewritten.
+    if (j > 0 && !mbar_wait(&p_empty[t], (j - 1) & 1, p.err, kDevErrMmaWait)) {
       ok = false;
       break;
     }
-    uint8_t* pr = prow + pb * P_BYTES;
+    // New reference max only when some row's max grew past the threshold
+    // (warp-uniform, since the O rescale below uses warp-collective tcgen05.ld/st).
+    // Rows whose max did not move get alpha = 1.
+    const bool rescale = __any_sync(0xffffffffu, mx > m_used + kRescaleThreshold);
+    float alpha = 1.f;
+    if (rescale) {
+      const float m_new = fmaxf(m_used, mx);
+      alpha = ex2(m_used - m_new);  // 0 on the first tile (m_used = -inf)
+      l *= alpha;
+      m_used = m_new;
+    }
+    // p = 2^(s * scale_log2 - m): one FFMA + ex2 per score, packed to bf16 and
+    // stored 8 at a time (the scores die as the loop advances); row sum as 4 chains.
+    const float neg_m = -m_used;
+    float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < BN / 8; ++c) {
+      float e[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        e[u] = ex2(fmaf(s[8 * c + u], p.scale_log2, neg_m));
+        rs4[u & 3] += e[u];
+      }
       uint4 v;
-      v.x = pack_bf16x2(s[8 * c + 0], s[8 * c + 1]);
-      v.y = pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
-      v.z = pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
-      v.w = pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
-      *reinterpret_cast<uint4*>(pr + (c >> 3) * ATOM + (((c & 7) ^ sw) << 4)) = v;
+      v.x = pack_bf16x2(e[0], e[1]);
+      v.y = pack_bf16x2(e[2], e[3]);
+      v.z = pack_bf16x2(e[4], e[5]);
+      v.w = pack_bf16x2(e[6], e[7]);
+      *reinterpret_cast<uint4*>(prow + (c >> 3) * ATOM + (((c & 7) ^ sw) << 4)) = v;
+    }
+    l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+    // O_t *= alpha before P_t(j) V_j accumulates into it (the scores are dead here).
+    if (rescale && j > 0) {
+      tc_fence_after();
+      float o[32];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        tmem_ld32(tlane + o_col + c * 32, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+        tmem_st32(tlane + o_col + c * 32, o);
+      }
+      tmem_st_wait();
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&p_full[pb]);
+    if (lane == 0) mbar_arrive(&p_full[t]);
   }
 
   // ------------------------------ epilogue ------------------------------
-  const int qrow = qt * BM + row;
-  if (ok && n > 0 && mbar_wait(&p_empty[(n - 1) % NP], ((n - 1) / NP) & 1, p.err, kDevErrMmaWait)) {
+  const int qrow = (qt * NT + t) * BM + row;
+  if (ok && n > 0 && mbar_wait(&p_empty[t], (n - 1) & 1, p.err, kDevErrMmaWait)) {
     tc_fence_after();
     const float inv = l > 0.f ? 1.f / l : 0.f;
     __nv_bfloat16* orow = p.o + ((size_t)bh * p.Lq + qrow) * D;
 #pragma unroll
     for (int c = 0; c < D / 32; ++c) {
       float o[32];
-      tmem_ld32(tlane + 2 * BN + c * 32, o);
+      tmem_ld32(tlane + o_col + c * 32, o);
       tmem_ld_wait();
       if (qrow < p.Lq) {
 #pragma unroll
@@ -431,7 +442,7 @@ static int launch(const void* q, const void* k, const void* v, void* o, float* l
   p.scale_log2 = scale * 1.4426950408889634f;
   auto kern = fmha_fwd_kernel<D>;
   FK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
-  const dim3 grid((unsigned)((Lq + BM - 1) / BM), (unsigned)(B * H), 1);
+  const dim3 grid((unsigned)((Lq + NT * BM - 1) / (NT * BM)), (unsigned)(B * H), 1);
   kern<<<grid, NTHREADS, Cf::SMEM, stream>>>(tmQ, tmK, tmV, p);
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
