@@ -85,7 +85,32 @@ def case_tc_m128_rms_qkv(launches: int):
     _gemm_case(128, 6144, 4096, launches, "rms")
 
 
+def _prefill_case(D, launches):
+    from .prefill_attention import flash_attention
+
+    B, H, L = 2, 16, 4096
+    g = torch.Generator(device="cuda").manual_seed(D)
+    q, k, v = [(torch.randn(B, H, L, D, device="cuda", generator=g) + 0.5).bfloat16() for _ in range(3)]
+    o = torch.empty_like(q)
+    for _ in range(2 + launches):
+        flash_attention(q, k, v, o)
+    torch.cuda.synchronize()
+    print(f"prefill D={D}: B={B} H={H} L={L} flops={4 * B * H * L * L * D}")
+
+
+def case_prefill_d64(launches: int):
+    """Prefill attention, the reference test shape at 2 of 16 batches: [2, 16, 4096, 64]."""
+    _prefill_case(64, launches)
+
+
+def case_prefill_d128(launches: int):
+    """Prefill attention [2, 16, 4096, 128]."""
+    _prefill_case(128, launches)
+
+
 CASES = {
+    "prefill_d64": case_prefill_d64,
+    "prefill_d128": case_prefill_d128,
     "tc_m64": case_tc_m64,
     "tc_m128_rms_qkv": case_tc_m128_rms_qkv,
     "attn_small": case_attn_small,
