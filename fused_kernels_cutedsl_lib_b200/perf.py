@@ -155,14 +155,52 @@ def gemm_sweep(iters: int = 30, include_cublas: bool = True) -> list[dict]:
     return rows
 
 
+def prefill_sweep(iters: int = 20) -> list[dict]:
+    """Prefill attention at the reference's FlashSM90 test size ([16, 16, 4096, D],
+    attn/attempt6_epi_pipeline/tests.py:138-154), D = 64 and 128, against torch
+    SDPA's cuDNN and flash backends. Compute-bound: FLOPs = 4·B·H·Lq·Lkv·D;
+    the median of back-to-back launches (inputs stay in L2 as they would in a model)."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from .prefill_attention import flash_attention
+
+    peak = measured_peaks()
+    rows = []
+    for D in (64, 128):
+        B, H, L = 16, 16, 4096
+        g = torch.Generator(device="cuda").manual_seed(D)
+        q, k, v = [(torch.randn(B, H, L, D, device="cuda", generator=g) + 0.5).bfloat16() for _ in range(3)]
+        o = torch.empty_like(q)
+        flops = 4 * B * H * L * L * D
+        t = statistics.median(time_launches(lambda i: flash_attention(q, k, v, o), iters=iters))
+        row = {"kernel": "fmha_fwd", "B": B, "H": H, "L": L, "D": D, "ms": round(t, 4),
+               "TFLOPs": round(flops / t / 1e9, 1), "tensor_frac": round(flops / t / 1e9 / peak["bf16_tflops"], 3)}
+        for name, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+            try:
+                with sdpa_kernel([be]):
+                    tr = statistics.median(time_launches(
+                        lambda i: torch.nn.functional.scaled_dot_product_attention(q, k, v), iters=iters))
+                row[f"sdpa_{name}_ms"] = round(tr, 4)
+                row[f"sdpa_{name}_TFLOPs"] = round(flops / tr / 1e9, 1)
+            except RuntimeError as e:  # backend unavailable for this shape
+                row[f"sdpa_{name}"] = str(e).splitlines()[0][:80]
+        rows.append(row)
+    return rows
+
+
 def main():
     import argparse
 
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=30)
+    ap.add_argument("--only", choices=["gemm", "prefill"], default=None)
     args = ap.parse_args()
-    for r in gemm_sweep(args.iters):
-        print(json.dumps(r), flush=True)
+    if args.only in (None, "gemm"):
+        for r in gemm_sweep(args.iters):
+            print(json.dumps(r), flush=True)
+    if args.only in (None, "prefill"):
+        for r in prefill_sweep():
+            print(json.dumps(r), flush=True)
 
 
 if __name__ == "__main__":
