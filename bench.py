@@ -407,7 +407,7 @@ def run_layer(args):
     use_graph = not args.no_graph
     graphs = []
     if use_graph:
-        # One decode step (7 launches on 1 GPU; + 5 all-gathers under TP) captured
+        # One decode step (12 launches on 1 GPU; 13 + 5 all-gathers under TP) captured
         # once and replayed: no per-launch host work inside the timed loop.
         graphs = [torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()]
         with torch.cuda.graph(graphs[0]):
@@ -464,7 +464,10 @@ def run_layer(args):
             "peak_GBps": peak, "peak_kind": kind,
             "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
-            "gpu_launches": args.steps * (7 if world == 1 else 7),
+            # this library's kernels per step: QKV (rms_split, GEMM, reduce; KV append
+            # fused), attention (2), O-proj (GEMM, reduce), gate/up (rms_split, GEMM,
+            # reduce), down (GEMM, reduce); under TP the append is its own kernel
+            "gpu_launches": args.steps * (12 if world == 1 else 13),
             "clocks": clk,
         }), flush=True)
     # Graphs that captured NCCL collectives must be freed before the process
