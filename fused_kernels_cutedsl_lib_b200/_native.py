@@ -62,6 +62,23 @@ SIGNATURES: dict[str, tuple] = {
         _c_int,
         [_p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _p],
     ),
+    "fk_linear_ex": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _p, _c_int, _p, _c_int, _p, _c_int, _c_int, _c_int, _c_int, _c_float, _p,
+         ctypes.c_size_t, _p],
+    ),
+    "fk_dec_attn_fwd_peers": (
+        _c_int,
+        [_p, ctypes.c_longlong, _p, _p, _p, _p, _p, _c_int, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_int, _c_float, _p],
+    ),
+    "fk_peer_alloc": (_c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "fk_peer_free": (_c_int, [_p]),
+    "fk_ipc_handle_bytes": (_c_int, []),
+    "fk_ipc_get_handle": (_c_int, [_p, _p]),
+    "fk_ipc_open": (_c_int, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "fk_ipc_close": (_c_int, [_p]),
+    "fk_peer_barrier": (_c_int, [_p, _p, _p, _c_int, _c_int, _p]),
     "fk_lora_linear": (
         _c_int,
         [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p, ctypes.c_size_t, _p],

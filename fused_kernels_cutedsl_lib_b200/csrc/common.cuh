@@ -264,12 +264,31 @@ __device__ __forceinline__ void kv_append_store(const KvAppend& a, int m_local, 
   base[row * a.width + rel] = v;
 }
 
+// Output placement of a linear call: y and residual rows `ldy` / `ldr` elements
+// apart (0: N, dense), and up to kMaxPeers more copies of y written with plain
+// stores into other GPUs' memory (CUDA IPC mappings of their buffers) at the same
+// offsets: the GEMM's epilogue performs the all-gather of a column-parallel layer.
+constexpr int kMaxPeers = 7;
+struct OutPlace {
+  int ldy, ldr;
+  int npeers;
+  __nv_bfloat16* peer_y[kMaxPeers];
+};
+
+__device__ __forceinline__ void store_out_all(const OutPlace& o, __nv_bfloat16* y, size_t off, __nv_bfloat16 v) {
+  y[off] = v;
+#pragma unroll
+  for (int i = 0; i < kMaxPeers; ++i)  // constant indices: the pointers stay in the parameter bank
+    if (i < o.npeers) o.peer_y[i][off] = v;
+}
+
 // Extensions a linear call may carry besides its main operands.
 struct LinearExtras {
   KvAppend kv;                 // kv.k_cache null: none
   const void* lora_xa;         // [M, rank] bf16: x . A^T (null: no LoRA)
   const void* lora_b;          // [N, rank] bf16
   int lora_rank;               // multiple of 8
+  OutPlace out;                // ldy = ldr = 0, npeers = 0: dense local output
 };
 
 }  // namespace fk

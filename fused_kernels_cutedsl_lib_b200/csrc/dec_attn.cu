@@ -342,7 +342,8 @@ __global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ 
                                                       const int* __restrict__ seqlens,
                                                       __nv_bfloat16* __restrict__ out,
                                                       float* __restrict__ lse, int B, int Hq,
-                                                      int Lmax, int chunk, int* seqlens_commit) {
+                                                      int Lmax, int chunk, int* seqlens_commit,
+                                                      OutPlace peers) {
   // Launched as a programmatic dependent of pass 1: wait for its partials.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -380,6 +381,9 @@ __global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ 
   packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
   packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
   reinterpret_cast<uint2*>(out + (size_t)row * D)[lane] = packed;
+#pragma unroll
+  for (int i = 0; i < kMaxPeers; ++i)  // the same rows in other GPUs' buffers (all-gather of a batch shard)
+    if (i < peers.npeers) reinterpret_cast<uint2*>(peers.peer_y[i] + (size_t)row * D)[lane] = packed;
   if (lane == 0) lse[row] = ok ? M + logf(W) : -INFINITY;
 }
 
@@ -535,7 +539,8 @@ int fk_dec_attn_fwd_paged(const void* q, const void* k_pool, const void* v_pool,
 
 static int combine_impl(const float* o_partial, const float* lse_partial, const int32_t* cache_seqlens,
                         int32_t* seqlens_commit, void* out, float* lse, int batch, int max_seqlen,
-                        int num_heads_q, int head_dim, int num_splits, void* stream) {
+                        int num_heads_q, int head_dim, int num_splits, void* stream,
+                        const OutPlace& peers = OutPlace{}) {
   FK_CHECK_ARG(o_partial && lse_partial && cache_seqlens && out && lse, "null tensor pointer");
   FK_CHECK_ARG(seqlens_commit != (int32_t*)cache_seqlens, "seqlens_commit must not alias cache_seqlens");
   FK_CHECK_ARG(batch >= 1 && max_seqlen >= 1 && num_heads_q >= 1 && num_splits >= 1,
@@ -556,7 +561,7 @@ static int combine_impl(const float* o_partial, const float* lse_partial, const 
   cfg.numAttrs = 1;
   FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn::combine_kernel, o_partial, lse_partial, cache_seqlens,
                                    static_cast<__nv_bfloat16*>(out), lse, batch, num_heads_q, max_seqlen,
-                                   chunk, seqlens_commit));
+                                   chunk, seqlens_commit, peers));
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -567,6 +572,24 @@ int fk_dec_attn_combine(const float* o_partial, const float* lse_partial,
                         void* stream) {
   return combine_impl(o_partial, lse_partial, cache_seqlens, nullptr, out, lse, batch, max_seqlen, num_heads_q,
                       head_dim, num_splits, stream);
+}
+
+int fk_dec_attn_fwd_peers(const void* q, long long q_batch_stride, const void* k_cache, const void* v_cache,
+                          const int32_t* cache_seqlens, void* out, void* const* peer_out, int npeers, float* lse,
+                          float* o_partial, float* lse_partial, int batch, int max_seqlen, int num_heads_q,
+                          int num_heads_kv, int head_dim, int num_splits, float softmax_scale, void* stream) {
+  FK_CHECK_ARG(npeers >= 0 && npeers <= kMaxPeers, "npeers must be in [0, 7]");
+  OutPlace peers = {};
+  peers.npeers = npeers;
+  for (int i = 0; i < npeers; ++i) {
+    FK_CHECK_ARG(peer_out && peer_out[i] && ((uintptr_t)peer_out[i] & 7) == 0, "peer output must be 8-byte aligned");
+    peers.peer_y[i] = static_cast<__nv_bfloat16*>(peer_out[i]);
+  }
+  int rc = splitkv_fwd_impl(q, q_batch_stride, k_cache, v_cache, cache_seqlens, o_partial, lse_partial, batch,
+                            max_seqlen, num_heads_q, num_heads_kv, head_dim, num_splits, softmax_scale, stream);
+  if (rc) return rc;
+  return combine_impl(o_partial, lse_partial, cache_seqlens, nullptr, out, lse, batch, max_seqlen, num_heads_q,
+                      head_dim, num_splits, stream, peers);
 }
 
 int fk_dec_attn_fwd_commit(const void* q, long long q_batch_stride, const void* k_cache, const void* v_cache,

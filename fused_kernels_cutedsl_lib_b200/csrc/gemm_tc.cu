@@ -89,6 +89,7 @@ struct Params {
   int G;
   int KI_main;        // k blocks of x . W^T; blocks [KI_main, KI) are the LoRA segment
   KvAppend kv;
+  OutPlace out;       // row strides of y / residual and peer copies of y
   int starts[kMaxGrid + 1];  // starts[c] = c * total / G: first iteration of CTA c
 };
 
@@ -154,10 +155,9 @@ __device__ __forceinline__ void load_tokens(uint32_t trow, int c0, int Mp, float
 __device__ __forceinline__ void store_out(const Params& p, int m, int col, float g, float u, bool swiglu) {
   float rs = p.rstd ? __ldg(p.rstd + m) : 1.f;
   float val = swiglu ? silu_f(g * rs) * (u * rs) : g * rs;
-  const size_t off = (size_t)m * p.N + col;
-  if (p.residual) val += __bfloat162float(p.residual[off]);
+  if (p.residual) val += __bfloat162float(p.residual[(size_t)m * p.out.ldr + col]);
   const __nv_bfloat16 out = __float2bfloat16_rn(val);
-  p.y[off] = out;
+  store_out_all(p.out, p.y, (size_t)m * p.out.ldy + col, out);
   kv_append_store(p.kv, m, col, out);
 }
 
@@ -619,6 +619,8 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   p.KI_main = KI_main;
   p.kv = {};
   if (ex) p.kv = ex->kv;
+  const OutPlace out0 = ex ? ex->out : OutPlace{};
+  const int ldy = out0.ldy > 0 ? out0.ldy : N, ldr = out0.ldr > 0 ? out0.ldr : N;
   p.partials = reinterpret_cast<float*>(ws + kCounterBytes + tc_xs_bytes(K) + tc_rstd_bytes());
   p.err = err;
   p.N = N;
@@ -687,8 +689,12 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
                     CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     p.M = mt;
-    p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * N;
-    p.residual = residual ? static_cast<const __nv_bfloat16*>(residual) + (size_t)m0 * N : nullptr;
+    p.y = static_cast<__nv_bfloat16*>(y) + (size_t)m0 * ldy;
+    p.residual = residual ? static_cast<const __nv_bfloat16*>(residual) + (size_t)m0 * ldr : nullptr;
+    p.out = out0;
+    p.out.ldy = ldy;
+    p.out.ldr = ldr;
+    for (int i = 0; i < out0.npeers; ++i) p.out.peer_y[i] = out0.peer_y[i] + (size_t)m0 * ldy;
     CUtensorMap tmXa = tmX;
     if (lora) {
       const uint64_t adims[2] = {(uint64_t)ex->lora_rank, (uint64_t)mt};

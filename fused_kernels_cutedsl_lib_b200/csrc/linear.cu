@@ -124,4 +124,24 @@ int fk_linear_kv_append(const void* x, const void* gamma, const void* w, void* y
   return dispatch(x, gamma, w, nullptr, 0, nullptr, y, M, N, K, eps, workspace, workspace_bytes, stream, &ex);
 }
 
+// General linear with output placement: y rows ldy apart (>= N), residual rows
+// ldr apart, and npeers more copies of y in other GPUs' memory (IPC mappings).
+int fk_linear_ex(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
+                 const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M, int N,
+                 int K, float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  FK_CHECK_ARG(npeers >= 0 && npeers <= kMaxPeers, "npeers must be in [0, 7]");
+  FK_CHECK_ARG(ldy == 0 || ldy >= N, "ldy must be 0 (dense) or >= N");
+  FK_CHECK_ARG(ldr == 0 || ldr >= N, "ldr must be 0 (dense) or >= N");
+  LinearExtras ex = {};
+  ex.out.ldy = ldy;
+  ex.out.ldr = ldr;
+  ex.out.npeers = npeers;
+  for (int i = 0; i < npeers; ++i) {
+    FK_CHECK_ARG(peer_y && peer_y[i], "null peer output pointer");
+    ex.out.peer_y[i] = static_cast<__nv_bfloat16*>(peer_y[i]);
+  }
+  return dispatch(x, gamma, w, w_up, up_row_offset, residual, y, M, N, K, eps, workspace, workspace_bytes, stream,
+                  &ex);
+}
+
 }  // extern "C"

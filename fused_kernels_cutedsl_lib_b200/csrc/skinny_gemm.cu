@@ -81,6 +81,7 @@ struct Params {
   int G;
   float eps, inv_k;
   KvAppend kv;
+  OutPlace out;                   // row strides of y / residual and peer copies of y
 };
 
 __device__ __forceinline__ long long it_start(const Params& p, int c) {
@@ -416,10 +417,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int col = col0 + (e >> 1) * 8;
           if (m < p.M && col < p.N) {
             float val = SWIGLU ? silu_f(v[0][t][e]) * v[NMAT - 1][t][e] : v[0][t][e];
-            const size_t off = (size_t)m * p.N + col;
-            if (p.residual) val += __bfloat162float(p.residual[off]);
+            if (p.residual) val += __bfloat162float(p.residual[(size_t)m * p.out.ldr + col]);
             const __nv_bfloat16 out = __float2bfloat16_rn(val);
-            p.y[off] = out;
+            store_out_all(p.out, p.y, (size_t)m * p.out.ldy + col, out);
             kv_append_store(p.kv, m, col, out);
           }
         }
@@ -503,10 +503,14 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   p.KI = KI_all;
   p.KI_main = KI_main;
   p.kv = {};
+  p.out = {};
   if (ex) {
     p.kv = ex->kv;
     p.kv.m_base = 0;
+    p.out = ex->out;
   }
+  if (p.out.ldy <= 0) p.out.ldy = N;
+  if (p.out.ldr <= 0) p.out.ldr = N;
   p.num_rb = num_rb;
   p.up_row_offset = up_row_offset;
   p.total = (long long)num_rb * p.KI;

@@ -21,6 +21,7 @@ all-gathered over rows.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -314,3 +315,120 @@ class TPDecodeLayer:
                                               torch.empty(B, w.w_gate_up.shape[0] // 2, **dt)))
         return self._gather_cols(ops.linear(gu, w.w_down, torch.empty(B, c_hi - c_lo, **dt),
                                             residual=h[:, c_lo:c_hi].contiguous()))
+
+
+def _vp(ptrs):
+    arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+    return arr, len(ptrs)
+
+
+class PeerTPDecodeLayer:
+    """Tensor-parallel decode step whose all-gathers are done by the kernels.
+
+    Same sharding and results as :class:`TPDecodeLayer`, but each column-parallel
+    GEMM stores its output block straight into the full ``[B, n]`` activation
+    buffer of every rank (``fk_linear_ex`` with peer outputs: CUDA IPC mappings
+    of a :class:`~fused_kernels_cutedsl_lib_b200.peer.PeerArena`), and attention's
+    pass 2 stores this rank's batch rows into every rank's buffer
+    (``fk_dec_attn_fwd_peers``). A one-thread stage barrier (``fk_peer_barrier``)
+    separates the stages. Per step: no NCCL call, no re-layout copy; 5 barriers.
+    Buffers are allocated once per batch size; steady-state calls allocate
+    nothing and can be captured in a CUDA graph.
+    """
+
+    def __init__(self, weights: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.w = weights
+        self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
+        self.hidden = weights.w_qkv.shape[1]
+        self.n_qkv = weights.w_qkv.shape[0] * self.world
+        self.ffn = weights.w_gate_up.shape[0] // 2 * self.world
+        self.qkv_lo = column_range(self.n_qkv, self.rank, self.world)[0]
+        self.c_lo = column_range(self.hidden, self.rank, self.world)[0]
+        self.f_lo = column_range(self.ffn, self.rank, self.world)[0]
+        self.arena = None
+        self._bufs: dict = {}
+
+    def _setup(self, B: int, Bl: int, L: int, device):
+        from .peer import PeerArena
+
+        key = (B, Bl, L)
+        if key in self._bufs:
+            return self._bufs[key]
+        H, F = self.hidden, self.ffn
+        if self.arena is None:
+            self.arena = PeerArena(2 * B * (self.n_qkv + self.hq * HEAD_DIM + 2 * H + F) + (1 << 16), self.group)
+        a = self.arena
+        S = default_num_splits(Bl, self.hkv, L)
+        o_p, l_p = alloc_partials(Bl, self.hq, S, device)
+        ws_need = max(workspace_bytes(B, n, k, sw) for n, k, sw in [
+            (self.w.w_qkv.shape[0], H, False), (self.w.w_o.shape[0], self.hq * HEAD_DIM, False),
+            (self.w.w_gate_up.shape[0] // 2, H, True), (self.w.w_down.shape[0], F, False)])
+        b = dict(qkv=a.region(f"qkv{B}", (B, self.n_qkv)), attn=a.region(f"attn{B}", (B, self.hq * HEAD_DIM)),
+                 h=a.region(f"h{B}", (B, H)), gu=a.region(f"gu{B}", (B, F)), y=a.region(f"y{B}", (B, H)),
+                 S=S, o_p=o_p, l_p=l_p, lse=torch.empty(Bl, self.hq, dtype=torch.float32, device=device),
+                 ws=alloc_workspace(ws_need, device))
+        self._bufs[key] = b
+        return b
+
+    def _linear(self, x, w, out_region, name, col_lo, n_total, b, *, gamma=None, w_up=None, up_row_offset=0,
+                residual=None, ldr=0):
+        M, K = x.shape
+        N = w.shape[0] - up_row_offset if w_up is not None else w.shape[0]
+        peers, n = _vp(self.arena.peer_ptrs(name, col_lo))
+        ws = b["ws"]
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        _native.check(_native.load().fk_linear_ex(
+            ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(w_up) if w_up is not None else None,
+            up_row_offset, residual, ldr, out_region.data_ptr() + 2 * col_lo, n_total, peers, n, M, N, K,
+            float(self.eps), ptr(ws), ws.numel(), ctypes.c_void_p(st)))
+
+    def __call__(self, x, k_cache, v_cache, cache_seqlens):
+        """x [B, H] replicated; k/v caches and lengths hold this rank's B/P rows. Returns y [B, H] (arena view)."""
+        B, Bl, L = x.shape[0], k_cache.shape[0], k_cache.shape[1]
+        if Bl * self.world != B:
+            raise ValueError(f"batch {B} must split evenly: {Bl} rows per rank x {self.world} ranks")
+        b = self._setup(B, Bl, L, x.device)
+        w, a, H, F = self.w, self.arena, self.hidden, self.ffn
+        B_ = str(B)
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        # QKV: this rank's column block of every row, pushed to all ranks
+        self._linear(x, w.w_qkv, b["qkv"], "qkv" + B_, self.qkv_lo, self.n_qkv, b, gamma=w.gamma_attn)
+        a.barrier()
+        # attention on this rank's batch rows (q read in place), rows pushed to all ranks
+        r0 = self.rank * Bl
+        my_qkv = b["qkv"][r0:r0 + Bl]
+        kv_append(my_qkv, k_cache, v_cache, cache_seqlens, self.hq, self.hkv)
+        hd = self.hq * HEAD_DIM
+        peers, n = _vp(a.peer_ptrs("attn" + B_, r0 * hd))
+        scale = 1.0 / math.sqrt(HEAD_DIM)
+        _native.check(_native.load().fk_dec_attn_fwd_peers(
+            ptr(my_qkv), my_qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens),
+            b["attn"].data_ptr() + 2 * r0 * hd, peers, n, ptr(b["lse"]), ptr(b["o_p"]), ptr(b["l_p"]), Bl, L,
+            self.hq, self.hkv, HEAD_DIM, b["S"], scale, ctypes.c_void_p(st)))
+        a.barrier()
+        # O-projection + residual x
+        self._linear(b["attn"], w.w_o, b["h"], "h" + B_, self.c_lo, H, b, residual=x.data_ptr() + 2 * self.c_lo,
+                     ldr=H)
+        a.barrier()
+        # RMSNorm -> gate/up -> SwiGLU
+        fl = w.w_gate_up.shape[0] // 2
+        self._linear(b["h"], w.w_gate_up, b["gu"], "gu" + B_, self.f_lo, F, b, gamma=w.gamma_ffn,
+                     w_up=w.w_gate_up, up_row_offset=fl)
+        a.barrier()
+        # down-projection + residual h
+        self._linear(b["gu"], w.w_down, b["y"], "y" + B_, self.c_lo, H, b,
+                     residual=b["h"].data_ptr() + 2 * self.c_lo, ldr=H)
+        a.barrier()
+        return b["y"]
+
+    def close(self):
+        if self.arena is not None:
+            self.arena.close()
+            self.arena = None
+            self._bufs.clear()

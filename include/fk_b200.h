@@ -258,6 +258,46 @@ FK_API int fk_linear_kv_append(const void* x, const void* gamma, const void* w, 
                                int num_heads_kv, int head_dim, int max_seqlen, int block_size, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* ---- tensor-parallel decode step over peer memory (one process per GPU) ----
+ * A column-parallel GEMM writes its output block into the full activation
+ * buffer of every rank from its epilogue (plain stores through CUDA IPC
+ * mappings), and fk_peer_barrier orders the ranks between stages: together they
+ * replace the all-gather + re-layout of an NCCL layer. */
+
+/* fk_linear with output placement: y rows ldy (0: N) elements apart, residual
+ * rows ldr (0: N) apart, and npeers (<= 7) more copies of y at peer_y[i] (other
+ * GPUs' buffers, same offsets). */
+FK_API int fk_linear_ex(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
+                        const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M,
+                        int N, int K, float eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* fk_dec_attn_fwd_ex whose pass 2 also writes each output row to peer_out[i]
+ * (npeers <= 7 other GPUs' buffers, same offsets): the all-gather of a
+ * batch-sharded attention output. */
+FK_API int fk_dec_attn_fwd_peers(const void* q, long long q_batch_stride, const void* k_cache, const void* v_cache,
+                                 const int32_t* cache_seqlens, void* out, void* const* peer_out, int npeers,
+                                 float* lse, float* o_partial, float* lse_partial, int batch, int max_seqlen,
+                                 int num_heads_q, int num_heads_kv, int head_dim, int num_splits,
+                                 float softmax_scale, void* stream);
+
+/* Zero-filled device buffer that can be shared through CUDA IPC, and its release. */
+FK_API int fk_peer_alloc(size_t bytes, void** ptr_out);
+FK_API int fk_peer_free(void* ptr);
+/* Size of an IPC handle; export a buffer's handle; map / unmap a peer's buffer. */
+FK_API int fk_ipc_handle_bytes(void);
+FK_API int fk_ipc_get_handle(void* ptr, void* handle_out);
+FK_API int fk_ipc_open(const void* handle, void** ptr_out);
+FK_API int fk_ipc_close(void* ptr);
+
+/* Stage barrier among nranks GPUs: one thread advances *counter to seq, fences
+ * at system scope (ordering every earlier write of this stream, peer stores
+ * included), stores seq into peer_flags[r][rank] for every r != rank and waits
+ * (at most 1 s, then the device error word is set) until local_flags[r] >= seq
+ * for every r != rank. counter and local_flags live in this GPU's memory;
+ * peer_flags[r] is rank r's flags array mapped here. */
+FK_API int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer_flags, int rank,
+                           int nranks, void* stream);
+
 /* Skinny GEMM y = x W^T (1 <= M <= 16, N <= 524288) that allocates nothing:
  * its stream-K scratch is a fixed ~2.7 MB device array inside this library
  * (one per GPU, kept until process exit) instead of a caller workspace. For

@@ -71,3 +71,83 @@ def test_tp2_layer_matches_oracle():
         assert derr == 0
         assert mx <= 5e-2 and mean <= 1e-2, (mx, mean)  # chained bound, as for the single-GPU layer
         assert lens == [251 + 3 * i for i in range(r * 8, r * 8 + 8)]
+
+
+def _peer_worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+
+        from fused_kernels_cutedsl_lib_b200 import _native
+        from fused_kernels_cutedsl_lib_b200.layer import (PeerTPDecodeLayer, TPDecodeLayer, random_layer_weights,
+                                                          shard_layer_weights)
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        res = {}
+        for B in (8, 64):  # skinny (M <= 16) and tcgen05 GEMM paths
+            L, H, F, HQ, HKV = 300, 1024, 2048, 16, 4
+            full = random_layer_weights(H, F, HQ, HKV, seed=21, device=dev)
+            shard = shard_layer_weights(full, rank, world, HQ, HKV)
+            g = torch.Generator(device=dev).manual_seed(22)
+            x = torch.randn(B, H, generator=g, device=dev).bfloat16()
+            Bl = B // world
+            k = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
+            v = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
+            lens = torch.tensor([200 + 5 * i for i in range(B)], dtype=torch.int32, device=dev)
+            rows = slice(rank * Bl, (rank + 1) * Bl)
+            kn, vn, ln = k[rows].contiguous(), v[rows].contiguous(), lens[rows].contiguous()
+            kp, vp, lp = kn.clone(), vn.clone(), ln.clone()
+            nccl_layer = TPDecodeLayer(shard, num_heads_q=HQ, num_heads_kv=HKV)
+            peer_layer = PeerTPDecodeLayer(shard, num_heads_q=HQ, num_heads_kv=HKV)
+            same = True
+            xn = xp = x
+            for _ in range(2):  # two eager steps, each feeding y back as x
+                xn = nccl_layer(xn, kn, vn, ln).clone()
+                xp = peer_layer(xp, kp, vp, lp).clone()
+                torch.cuda.synchronize()
+                same &= torch.equal(xn, xp)
+            # CUDA graph of one peer step, replayed: the barrier counter lives on the device
+            xg = xp.clone()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                yg = peer_layer(xg, kp, vp, lp)
+            for _ in range(3):
+                xn = nccl_layer(xn, kn, vn, ln).clone()
+                graph.replay()
+                torch.cuda.synchronize()
+                same &= torch.equal(xn, yg)
+                xg.copy_(yg)
+            del graph
+            same &= torch.equal(kn, kp) and torch.equal(vn, vp) and torch.equal(ln, lp)
+            peer_layer.close()
+            res[B] = same
+        q.put((rank, res, _native.device_error()))
+        dist.destroy_process_group()
+    except Exception as e:
+        import traceback
+        q.put((rank, repr(e) + traceback.format_exc()[-800:], None))
+
+
+@needs_2
+def test_tp2_peer_memory_layer_matches_nccl_layer():
+    """GEMM epilogues and attention pass 2 push their output blocks into every
+    rank's buffer (CUDA IPC), with a stage barrier kernel: bit-identical to the
+    NCCL all-gather layer, eager and under CUDA-graph replay."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r[0]: r for r in (q.get(timeout=300) for _ in procs)}
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        _, same, derr = res[r]
+        assert isinstance(same, dict), same
+        assert derr == 0
+        assert all(same.values()), same
