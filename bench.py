@@ -366,8 +366,8 @@ def run_layer(args):
     import torch.distributed as dist
 
     from fused_kernels_cutedsl_lib_b200 import _native
-    from fused_kernels_cutedsl_lib_b200.layer import (DecodeLayer, TPDecodeLayer, random_layer_weights,
-                                                      shard_layer_weights)
+    from fused_kernels_cutedsl_lib_b200.layer import (DecodeLayer, PeerTPDecodeLayer, TPDecodeLayer,
+                                                      random_layer_weights, shard_layer_weights)
 
     world, rank, local = _dist()
     torch.cuda.set_device(local)
@@ -384,7 +384,9 @@ def run_layer(args):
     lens = torch.full((Bl,), ctx, dtype=torch.int32, device=dev)
     gx = torch.Generator(device=dev).manual_seed(44)
     x = torch.randn(B, H, generator=gx, device=dev).to(torch.bfloat16)
-    if world > 1:
+    if world > 1 and args.tp_mode == "peer":
+        layer = PeerTPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
+    elif world > 1:
         layer = TPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
     else:
         layer = DecodeLayer(full, HQ, HKV)
@@ -456,7 +458,10 @@ def run_layer(args):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights seed 4, N(0,1) KV)",
             "config": {"workload": "decode_layer_config5", "batch": B, "context": ctx, "hidden": H, "ffn": F,
                        "heads_q": HQ, "heads_kv": HKV,
-                       "parallelism": "single GPU" if world == 1 else f"tp{world} GEMMs + batch-sharded attention",
+                       "parallelism": "single GPU" if world == 1 else (
+                           f"tp{world} GEMMs + batch-sharded attention, all-gathers "
+                           + ("in the GEMM / attention epilogues over peer memory" if args.tp_mode == "peer"
+                              else "by NCCL")),
                        "cuda_graph": not args.no_graph,
                        "l2": "weights 436 MB + KV 4.3 GB per step exceed L2"},
             "bytes_per_step": wbytes + kv_bytes,
@@ -467,7 +472,7 @@ def run_layer(args):
             # this library's kernels per step: QKV (rms_split, GEMM, reduce; KV append
             # fused), attention (2), O-proj (GEMM, reduce), gate/up (rms_split, GEMM,
             # reduce), down (GEMM, reduce); under TP the append is its own kernel
-            "gpu_launches": args.steps * (12 if world == 1 else 13),
+            "gpu_launches": args.steps * (12 if world == 1 else (18 if args.tp_mode == "peer" else 13)),
             "clocks": clk,
         }), flush=True)
     # Graphs that captured NCCL collectives must be freed before the process
@@ -476,6 +481,9 @@ def run_layer(args):
     graphs.clear()
     torch.cuda.synchronize()
     if world > 1:
+        dist.barrier()
+        if hasattr(layer, "close"):
+            layer.close()  # unmap the peers' buffers before the ranks exit
         dist.barrier()
         dist.destroy_process_group()
 
@@ -489,6 +497,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="layer workload: launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--tp-mode", choices=["peer", "nccl"], default="peer",
+                    help="layer workload on N > 1 GPUs: all-gathers in the kernels over peer memory, or by NCCL")
     ap.add_argument("--workload", choices=["attention", "layer"], default="attention",
                     help="attention: config 2 split-KV decode attention (headline); layer: config 5 decode step")
     args = ap.parse_args()
