@@ -39,16 +39,16 @@ def _gemm_case(M, N, K, launches, kind="plain"):
     from . import configs
     from .gemm import alloc_workspace, linear, workspace_bytes
 
-    rows = 2 * N if kind == "swiglu" else N
+    rows = 2 * N if kind in ("swiglu", "rms_swiglu") else N
     x, w = configs.gemm_inputs(M, rows, K, 2)
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-    gamma = torch.ones(K, dtype=torch.bfloat16, device="cuda") if kind == "rms" else None
-    ws = alloc_workspace(workspace_bytes(M, N, K, kind == "swiglu"), "cuda")
+    gamma = torch.ones(K, dtype=torch.bfloat16, device="cuda") if kind in ("rms", "rms_swiglu") else None
+    ws = alloc_workspace(workspace_bytes(M, N, K, kind in ("swiglu", "rms_swiglu")), "cuda")
     flush = torch.empty(256 << 18, dtype=torch.int32, device="cuda")  # 256 MB L2 flush
     for _ in range(2 + launches):
         flush.fill_(0)
-        if kind == "swiglu":
-            linear(x, w, y, w_up=w, up_row_offset=N, workspace=ws)
+        if kind in ("swiglu", "rms_swiglu"):
+            linear(x, w, y, gamma=gamma, w_up=w, up_row_offset=N, workspace=ws)
         else:
             linear(x, w, y, gamma=gamma, workspace=ws)
     torch.cuda.synchronize()
@@ -73,6 +73,11 @@ def case_tc_m256(launches: int):
 def case_tc_m128_swiglu(launches: int):
     """tcgen05 SwiGLU gate/up GEMM, config 4 at M=128: W [28672, 4096] = 235 MB."""
     _gemm_case(128, 14336, 4096, launches, "swiglu")
+
+
+def case_tc_m128_rms_swiglu(launches: int):
+    """tcgen05 RMSNorm->gate/up->SwiGLU GEMM (the layer's FFN input), M=128: 256 token columns (hi/lo)."""
+    _gemm_case(128, 14336, 4096, launches, "rms_swiglu")
 
 
 def case_tc_m64(launches: int):
@@ -118,6 +123,7 @@ CASES = {
     "skinny_m1": case_skinny_m1,
     "tc_m256": case_tc_m256,
     "tc_m128_swiglu": case_tc_m128_swiglu,
+    "tc_m128_rms_swiglu": case_tc_m128_rms_swiglu,
 }
 
 

@@ -284,3 +284,25 @@ def test_lora_argument_errors():
     lb = torch.zeros(256, 16, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):
         lora_linear(x, w, lb)  # neither lora_a nor lora_xa
+
+
+# ---- output placement (row strides of y / residual), used by the tensor-parallel layer ----
+
+@pytest.mark.parametrize("M", [4, 100])
+def test_linear_ex_strided_output_and_residual(M):
+    import ctypes
+
+    N, K, ld = 512, 256, 1536
+    x, w = mk(M, N, K, seed=M)
+    full = torch.full((M, ld), 7.0, dtype=torch.bfloat16, device="cuda")  # [M, ld]; our block at columns 640..
+    res_full = torch.randn(M, ld, device="cuda").bfloat16()
+    c0 = 640
+    ws = alloc_workspace(workspace_bytes(M, N, K), "cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _native.check(_native.load().fk_linear_ex(
+        x.data_ptr(), None, w.data_ptr(), None, 0, res_full.data_ptr() + 2 * c0, ld, full.data_ptr() + 2 * c0, ld,
+        None, 0, M, N, K, 0.0, ws.data_ptr(), ws.numel(), ctypes.c_void_p(st)))
+    finish()
+    ref = linear(x, w, residual=res_full[:, c0:c0 + N].contiguous())
+    assert torch.equal(full[:, c0:c0 + N], ref)
+    assert torch.all(full[:, :c0] == 7.0) and torch.all(full[:, c0 + N:] == 7.0)
