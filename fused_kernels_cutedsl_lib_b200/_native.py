@@ -7,10 +7,12 @@ entry point raises. Build it with ``python -m fused_kernels_cutedsl_lib_b200.bui
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libfk_b200.so"
+# FK_LIB_PATH selects another build of the same library (A/B measurements).
+LIB_PATH = Path(os.environ.get("FK_LIB_PATH") or Path(__file__).resolve().parent / "_lib" / "libfk_b200.so")
 
 _c_int = ctypes.c_int
 _c_float = ctypes.c_float

@@ -90,6 +90,7 @@ struct Params {
   int KI_main;        // k blocks of x . W^T; blocks [KI_main, KI) are the LoRA segment
   KvAppend kv;
   OutPlace out;       // row strides of y / residual and peer copies of y
+  int has_ext;        // peers or KV append present (store_ext needed)
   int starts[kMaxGrid + 1];  // starts[c] = c * total / G: first iteration of CTA c
 };
 
@@ -152,13 +153,22 @@ __device__ __forceinline__ void load_tokens(uint32_t trow, int c0, int Mp, float
   }
 }
 
-__device__ __forceinline__ void store_out(const Params& p, int m, int col, float g, float u, bool swiglu) {
+// Final value of output (m, col): RMSNorm scale, SwiGLU, residual, bf16; stored to y.
+__device__ __forceinline__ __nv_bfloat16 store_out(const Params& p, int m, int col, float g, float u, bool swiglu) {
   float rs = p.rstd ? __ldg(p.rstd + m) : 1.f;
   float val = swiglu ? silu_f(g * rs) * (u * rs) : g * rs;
   if (p.residual) val += __bfloat162float(p.residual[(size_t)m * p.out.ldr + col]);
   const __nv_bfloat16 out = __float2bfloat16_rn(val);
-  store_out_all(p.out, p.y, (size_t)m * p.out.ldy + col, out);
-  kv_append_store(p.kv, m, col, out);
+  p.y[(size_t)m * p.out.ldy + col] = out;
+  return out;
+}
+// The optional extra destinations of a stored value (peer copies, KV-cache
+// append). Kept out of the per-element store above and run in a separate loop
+// only when a call has them: inlined into every store they cost 5-15 % of the
+// GEMM through code size.
+__device__ __forceinline__ void store_ext(const Params& p, int m, int col, __nv_bfloat16 v) {
+  store_out_all(p.out, p.y, (size_t)m * p.out.ldy + col, v);  // rewrites y too (same value)
+  kv_append_store(p.kv, m, col, v);
 }
 
 template <int NMMA, bool SWIGLU, bool NORM>
@@ -368,9 +378,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         load_tokens<NORM>(trow, c0, p.Mp, a);
         if (SWIGLU) load_tokens<NORM>(trow + NMMA, c0, p.Mp, u);
         if (col < p.N) {
+          __nv_bfloat16 o[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            if (c0 + i < p.M) store_out(p, c0 + i, col, a[i], SWIGLU ? u[i] : 0.f, SWIGLU);
+            if (c0 + i < p.M) o[i] = store_out(p, c0 + i, col, a[i], SWIGLU ? u[i] : 0.f, SWIGLU);
+          if (p.has_ext) {
+            for (int i = 0; i < 16 && c0 + i < p.M; ++i) store_ext(p, c0 + i, col, o[i]);
+          }
         }
       }
       tc_fence_before();
@@ -514,9 +528,13 @@ __global__ void __launch_bounds__(128) tc_reduce_kernel(Params p) {
   }
   const int col = rb * BM + row;
   if (col >= p.N) return;
+  __nv_bfloat16 o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    if (c0 + i < p.M) store_out(p, c0 + i, col, g[i], u[i], SWIGLU);
+    if (c0 + i < p.M) o[i] = store_out(p, c0 + i, col, g[i], u[i], SWIGLU);
+  if (p.has_ext) {
+    for (int i = 0; i < 8 && c0 + i < p.M; ++i) store_ext(p, c0 + i, col, o[i]);
+  }
 }
 
 template <int NMMA, bool SWIGLU, bool NORM>
@@ -695,6 +713,7 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
     p.out.ldy = ldy;
     p.out.ldr = ldr;
     for (int i = 0; i < out0.npeers; ++i) p.out.peer_y[i] = out0.peer_y[i] + (size_t)m0 * ldy;
+    p.has_ext = (out0.npeers > 0 || p.kv.k_cache != nullptr) ? 1 : 0;
     CUtensorMap tmXa = tmX;
     if (lora) {
       const uint64_t adims[2] = {(uint64_t)ex->lora_rank, (uint64_t)mt};

@@ -82,6 +82,7 @@ struct Params {
   float eps, inv_k;
   KvAppend kv;
   OutPlace out;                   // row strides of y / residual and peer copies of y
+  int has_ext;                    // peers or KV append present
 };
 
 __device__ __forceinline__ long long it_start(const Params& p, int c) {
@@ -409,6 +410,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (do_epilogue) {
       const int col0 = rb * RB + row;
+      __nv_bfloat16 o[NT][4];
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
@@ -418,11 +420,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (m < p.M && col < p.N) {
             float val = SWIGLU ? silu_f(v[0][t][e]) * v[NMAT - 1][t][e] : v[0][t][e];
             if (p.residual) val += __bfloat162float(p.residual[(size_t)m * p.out.ldr + col]);
-            const __nv_bfloat16 out = __float2bfloat16_rn(val);
-            store_out_all(p.out, p.y, (size_t)m * p.out.ldy + col, out);
-            kv_append_store(p.kv, m, col, out);
+            o[t][e] = __float2bfloat16_rn(val);
+            p.y[(size_t)m * p.out.ldy + col] = o[t][e];
           }
         }
+      // Extra destinations (peer copies, KV append) in their own loop, only when
+      // present: inlined into every store above they slow the kernel through code size.
+      if (p.has_ext) {
+        for (int t = 0; t < NT; ++t)
+          for (int e = 0; e < 4; ++e) {
+            const int m = t * 8 + 2 * c + (e & 1);
+            const int col = col0 + (e >> 1) * 8;
+            if (m < p.M && col < p.N) {
+              store_out_all(p.out, p.y, (size_t)m * p.out.ldy + col, o[t][e]);
+              kv_append_store(p.kv, m, col, o[t][e]);
+            }
+          }
+      }
     }
   }
 }
@@ -511,6 +525,7 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   }
   if (p.out.ldy <= 0) p.out.ldy = N;
   if (p.out.ldr <= 0) p.out.ldr = N;
+  p.has_ext = (p.out.npeers > 0 || p.kv.k_cache != nullptr) ? 1 : 0;
   p.num_rb = num_rb;
   p.up_row_offset = up_row_offset;
   p.total = (long long)num_rb * p.KI;
