@@ -59,9 +59,12 @@ template <int NMMA, bool SWIGLU>
 struct Layout {
   static constexpr int W_BYTES = WBOX * (SWIGLU ? 2 : 1);
   static constexpr int X_BYTES = NMMA * 128;
-  static constexpr int SX = (X_BYTES >= 32768 && SWIGLU) ? 2 : (X_BYTES >= 16384 ? 3 : 4);
+  static constexpr int SX = X_BYTES >= 32768 ? (SWIGLU ? 2 : 3) : (X_BYTES >= 16384 ? 5 : 6);
   static constexpr int SW_FIT = (int)((kSmemBudget - 4096 - (size_t)SX * X_BYTES) / (W_BYTES + 16));
-  static constexpr int SW = SW_FIT > 8 ? 8 : SW_FIT;
+  // As many weight stages as shared memory holds: the kernel streams at the
+  // rate of (weight bytes in flight per SM) / (HBM latency under load), so a
+  // deeper ring is directly faster.
+  static constexpr int SW = SW_FIT > 16 ? 16 : SW_FIT;
   static constexpr int STAGES = SW;
   static constexpr int X_RING = SW * W_BYTES;
   static constexpr int ACC_COLS = NMMA * (SWIGLU ? 2 : 1);
