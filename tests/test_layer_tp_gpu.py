@@ -86,8 +86,8 @@ def _peer_worker(rank, world, port, q):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
         res = {}
-        for B in (8, 64):  # skinny (M <= 16) and tcgen05 GEMM paths
-            L, H, F, HQ, HKV = 300, 1024, 2048, 16, 4
+        for B in (2 * world if world <= 8 else 16, 64):  # skinny (M <= 16) and tcgen05 GEMM paths
+            L, H, F, HQ, HKV = 300, 1024 * max(1, world // 2), 2048 * max(1, world // 2), 16, 8
             full = random_layer_weights(H, F, HQ, HKV, seed=21, device=dev)
             shard = shard_layer_weights(full, rank, world, HQ, HKV)
             g = torch.Generator(device=dev).manual_seed(22)
@@ -131,22 +131,24 @@ def _peer_worker(rank, world, port, q):
 
 
 @needs_2
-def test_tp2_peer_memory_layer_matches_nccl_layer():
+def test_tp_peer_memory_layer_matches_nccl_layer():
     """GEMM epilogues and attention pass 2 push their output blocks into every
     rank's buffer (CUDA IPC), with a stage barrier kernel: bit-identical to the
-    NCCL all-gather layer, eager and under CUDA-graph replay."""
+    NCCL all-gather layer, eager and under CUDA-graph replay. Runs on every GPU
+    present (2 to 8 ranks)."""
     import torch.multiprocessing as mp
 
+    world = min(8, torch.cuda.device_count())
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {r[0]: r for r in (q.get(timeout=300) for _ in procs)}
     for p in procs:
         p.join(timeout=120)
-    for r in range(2):
+    for r in range(world):
         _, same, derr = res[r]
         assert isinstance(same, dict), same
         assert derr == 0
