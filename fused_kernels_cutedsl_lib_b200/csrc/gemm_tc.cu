@@ -653,6 +653,11 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   FK_CHECK_ARG(p.total < (1LL << 31), "problem too large for the iteration table");
   int G = num_sms();
   if (G > tc::kMaxGrid) G = tc::kMaxGrid;
+  // At least 8 k blocks per CTA: small GEMMs (the column shards of a
+  // tensor-parallel layer) otherwise split each row block over dozens of CTAs
+  // and pay more for the partials than for the weights (measured best of 4-32).
+  constexpr int kMinIters = 8;
+  if (p.total / kMinIters < G) G = p.total >= kMinIters ? (int)(p.total / kMinIters) : 1;
   if ((long long)G > p.total) G = (int)p.total;
   p.G = G;
   for (int c = 0; c <= G; ++c) p.starts[c] = (int)((long long)c * p.total / G);

@@ -113,7 +113,49 @@ def case_prefill_d128(launches: int):
     _prefill_case(128, launches)
 
 
+def case_tp4_rank_step(launches: int):
+    """One rank's kernels of the 4-way tensor-parallel layer step at config 5 on one GPU
+    (M = 128 tokens; QKV 1536, O 1024, gate/up 2 x 3584, down 1024 columns; attention
+    over the rank's 32 batch rows at context 8192). Peer copies and barriers omitted."""
+    from .decoding_attention import alloc_partials, default_num_splits
+    from .gemm import alloc_workspace, linear, workspace_bytes
+    from .layer import attention_from_qkv, kv_append, random_layer_weights, shard_layer_weights
+
+    world, rank, B, ctx = 4, 0, 128, 8192
+    w = shard_layer_weights(random_layer_weights(seed=4), rank, world)
+    Bl = B // world
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(B, 4096, device="cuda", generator=g).bfloat16()
+    k = torch.randn(Bl, ctx + 64, 8, 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn_like(k)
+    ws = alloc_workspace(workspace_bytes(B, 14336, 4096, True), "cuda")
+    bf = dict(dtype=torch.bfloat16, device="cuda")
+    qkv_loc = torch.empty(B, w.w_qkv.shape[0], **bf)             # this rank's column blocks
+    qkv_rows = torch.randn(Bl, 6144, device="cuda", generator=g).bfloat16()  # the rank's rows, all columns
+    attn_full, h_full = torch.randn(B, 4096, **bf), torch.randn(B, 4096, **bf)
+    gu_full = torch.randn(B, 14336, **bf)
+    attn_loc = torch.empty(Bl, 4096, **bf)
+    h_loc, y_loc = torch.empty(B, w.w_o.shape[0], **bf), torch.empty(B, w.w_down.shape[0], **bf)
+    fl = w.w_gate_up.shape[0] // 2
+    gu_loc = torch.empty(B, fl, **bf)
+    res_x, res_h = x[:, :h_loc.shape[1]].contiguous(), h_full[:, :h_loc.shape[1]].contiguous()
+    S = default_num_splits(Bl, 8, ctx + 64)
+    o_p, l_p = alloc_partials(Bl, 32, S, "cuda")
+    lse = torch.empty(Bl, 32, device="cuda")
+    for _ in range(2 + launches):
+        lens = torch.full((Bl,), ctx, dtype=torch.int32, device="cuda")
+        linear(x, w.w_qkv, qkv_loc, gamma=w.gamma_attn, workspace=ws)
+        kv_append(qkv_rows, k, v, lens, 32, 8)
+        attention_from_qkv(qkv_rows, k, v, lens, attn_loc, lse, o_p, l_p, S, 32, 8)
+        linear(attn_full, w.w_o, h_loc, residual=res_x, workspace=ws)
+        linear(h_full, w.w_gate_up, gu_loc, gamma=w.gamma_ffn, w_up=w.w_gate_up, up_row_offset=fl, workspace=ws)
+        linear(gu_full, w.w_down, y_loc, residual=res_h, workspace=ws)
+    torch.cuda.synchronize()
+    print("tp4 rank step: 12 kernels per step")
+
+
 CASES = {
+    "tp4_rank_step": case_tp4_rank_step,
     "prefill_d64": case_prefill_d64,
     "prefill_d128": case_prefill_d128,
     "tc_m64": case_tc_m64,
