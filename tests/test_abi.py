@@ -71,3 +71,35 @@ def test_tvm_ffi_module_loads_and_exports():
     for name in ("dec_attn_splitkv_fwd", "dec_attn_combine", "dattn1", "skinny_gemm", "rmsnorm_linear",
                  "swiglu_gemm", "swiglu_gemm2", "lora_gemm", "linear_workspace_bytes"):
         assert getattr(mod, name) is not None
+
+
+def test_new_entry_points_validate_before_launch():
+    """Prefill attention, LoRA, fused KV append, output placement and the peer
+    barrier reject bad arguments with a status, before any CUDA call."""
+    lib = _native.load()
+    # prefill: head_dim 96
+    assert lib.fk_prefill_attn_fwd(16, 16, 16, 16, None, 1, 2, 2, 8, 8, 96, 0.1, None) == -1
+    assert "head_dim" in lib.fk_last_error().decode()
+    # prefill: q heads not a multiple of kv heads
+    assert lib.fk_prefill_attn_fwd(16, 16, 16, 16, None, 1, 3, 2, 8, 8, 64, 0.1, None) == -1
+    # LoRA: rank 12 is not a multiple of 8
+    assert lib.fk_lora_linear(16, 16, 16, 16, None, 16, 4, 128, 128, 12, 256, 1 << 20, None) == -1
+    assert "rank" in lib.fk_last_error().decode()
+    # fused KV append: next lengths may not alias the input lengths
+    assert lib.fk_linear_kv_append(16, None, 16, 16, 4, 1536, 512, 0.0, 16, 16, None, 32, 32, 512, 1024, 2, 128,
+                                   64, 0, 256, 1 << 20, None) == -1
+    assert "alias" in lib.fk_last_error().decode()
+    # fused KV append: K and V column ranges overlap
+    assert lib.fk_linear_kv_append(16, None, 16, 16, 4, 1536, 512, 0.0, 16, 16, None, 32, 48, 512, 600, 2, 128,
+                                   64, 0, 256, 1 << 20, None) == -1
+    # output placement: too many peers, ldy < N
+    assert lib.fk_linear_ex(16, None, 16, None, 0, None, 0, 16, 0, None, 8, 4, 128, 128, 0.0, 256, 1 << 20,
+                            None) == -1
+    assert lib.fk_linear_ex(16, None, 16, None, 0, None, 0, 16, 64, None, 0, 4, 128, 128, 0.0, 256, 1 << 20,
+                            None) == -1
+    # peer barrier: 9 ranks
+    arr = (ctypes.c_void_p * 9)(*([16] * 9))
+    assert lib.fk_peer_barrier(16, 16, arr, 0, 9, None) == -1
+    # attention with lengths commit aliasing the lengths
+    assert lib.fk_dec_attn_fwd_commit(16, 4096, 16, 16, None, 32, 32, 16, 16, 16, 16, 1, 64, 0, 0, 32, 8, 128, 1,
+                                      0.1, None) != 0
