@@ -344,6 +344,8 @@ __global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ 
                                                       float* __restrict__ lse, int B, int Hq,
                                                       int Lmax, int chunk, int* seqlens_commit,
                                                       OutPlace peers) {
+  // The next kernel may launch now (it waits for this grid before reading).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // Launched as a programmatic dependent of pass 1: wait for its partials.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);

@@ -484,6 +484,8 @@ __global__ void __launch_bounds__(256) rms_split_kernel(const __nv_bfloat16* __r
 // GEMM grid has completed and its writes are visible.
 template <int NMMA, bool SWIGLU>
 __global__ void __launch_bounds__(128) tc_reduce_kernel(Params p) {
+  // The next kernel may launch now (it waits for this grid before reading).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int rb = blockIdx.x;
   const int c0 = blockIdx.y * 8;

@@ -7,7 +7,8 @@
 // landed" before the next stage reads the buffer. It replaces the all-gather
 // (plus the [P, B, n/P] -> [B, n] re-layout copy) of an NCCL-based layer.
 //
-// Barrier protocol (one thread): seq = ++counter (a per-rank device counter, so
+// Barrier protocol (one thread, after griddepcontrol.wait: the kernel is a
+// programmatic dependent of the producer): seq = ++counter (a per-rank device counter, so
 // CUDA-graph replays advance it); system-scope fence, so the stores of the
 // preceding kernels on this stream - including their stores into peer memory -
 // are ordered before the flag; store seq into flags[rank] of every peer; wait
@@ -34,6 +35,11 @@ struct BarrierArgs {
 };
 
 __global__ void barrier_kernel(BarrierArgs a) {
+  // Launched as a programmatic dependent: let the next kernel launch (a GEMM
+  // starts streaming its weights; it waits for this grid before reading x),
+  // then wait for the producing kernels on this stream to complete.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x != 0) return;
   const int seq = *a.counter + 1;
   *a.counter = seq;
@@ -122,8 +128,16 @@ int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer
   a.rank = rank;
   a.nranks = nranks;
   a.err = err;
-  peer::barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  FK_CHECK_CUDA(cudaGetLastError());
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, peer::barrier_kernel, a));
   return kOk;
 }
 
