@@ -2,14 +2,16 @@
 
 One step for a batch of B sequences, each generating one token:
 
-1. ``qkv = rms_norm(x, gamma_attn) @ W_qkv^T``      fused RMSNorm->QKV GEMM
-2. append the new K/V rows to the cache at ``cache_seqlens[b]``; lengths += 1
+1. ``qkv = rms_norm(x, gamma_attn) @ W_qkv^T``      fused RMSNorm->QKV GEMM, whose epilogue also
+2. appends the new K/V rows to the cache at ``cache_seqlens[b]`` (lengths += 1, published by attention)
 3. ``attn = softmax(q K^T / sqrt(d)) V``             split-KV attention, q read in place from qkv
 4. ``h = x + attn @ W_o^T``                          GEMM with residual epilogue
 5. ``gu = silu(g) * u`` for ``[g; u] = rms_norm(h, gamma_ffn) @ W_gu^T``   fused RMSNorm->gate/up->SwiGLU
 6. ``y = h + gu @ W_down^T``                         GEMM with residual epilogue
 
-Seven launches, no host synchronisation and no torch compute on the path.
+Twelve kernel launches (tcgen05 path: RMSNorm prologue, GEMM and split-row-block
+reduction per RMSNorm GEMM, GEMM and reduction per plain GEMM, two attention
+passes), no host synchronisation and no torch compute on the path.
 The reference has no layer composition; this follows the decode path's full
 layer configuration (hidden 4096, 32 q / 8 kv heads of 128, FFN 14336).
 
@@ -17,7 +19,10 @@ layer configuration (hidden 4096, 32 q / 8 kv heads of 128, FFN 14336).
 GEMMs are column-parallel (each rank holds 1/P of every weight's output
 features) with an NCCL all-gather of each GEMM's output, and attention is
 batch-parallel (each rank holds the KV cache of B/P rows), its output
-all-gathered over rows.
+all-gathered over rows. :class:`PeerTPDecodeLayer` computes the same step with
+the all-gathers done by the kernels themselves: each GEMM epilogue and
+attention's pass 2 store their output blocks into every rank's buffer over
+peer memory, with a stage barrier kernel between stages.
 """
 from __future__ import annotations
 
