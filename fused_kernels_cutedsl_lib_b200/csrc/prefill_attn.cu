@@ -16,15 +16,19 @@
 //               the O rescale (tcgen05.ld/st of the row) runs only when a
 //               warp's max grows by more than 2^8, otherwise P keeps the stale
 //               max, which the final 1/l normalisation cancels exactly. P_t(j)
-//               is rounded to bf16 into a 128B-swizzled tile for the next MMA.
+//               is rounded to bf16 pairs and written over S_t(j) in TMEM
+//               (tcgen05.st), where the P V MMA reads it as its A operand.
 //               Epilogue: O / l to bf16, LSE = (m + log2 l) ln 2.
 //   warp 8      TMA producer: both Q tiles once, then K_0, V_0, K_1, V_1, ...
 //               (128 keys each) through one ring shared by the two tiles
 //               (3-D tensor maps: keys past Lkv read as zero)
 //   warp 9      allocates TMEM (S_A | S_B | O_A | O_B); one lane issues
-//               tcgen05.mma: S_t(j) = Q_t K_j^T (both operands K-major), then
-//               O_t += P_t(j) V_j (P K-major from shared memory, V MN-major
-//               straight from the TMA tile), committing to mbarriers
+//               tcgen05.mma: per j and tile, O_t += P_t(j) V_j (A = P from
+//               TMEM, B = V MN-major straight from the TMA tile), then
+//               S_t(j+1) = Q_t K_{j+1}^T into the same columns. The tensor pipe
+//               runs in issue order, so S_t(j+1) overwrites P_t(j) only after
+//               it was read, and the completion of S_t(j+1) also means
+//               P_t(j) V_j is in O_t: the softmax never waits for it.
 // Every mbarrier wait is bounded (device error word + orderly exit).
 #include <math.h>
 
@@ -40,19 +44,17 @@ constexpr int BN = 128;  // keys per tile
 constexpr int NTHREADS = 320;
 constexpr int TMA_WARP = 8, MMA_WARP = 9;
 constexpr int ATOM = 128 * 128;  // one 128-row x 64-element bf16 swizzle block: 16 KB
-constexpr int P_BYTES = 2 * ATOM;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr size_t kSmemLimit = 227 * 1024;
 
 template <int D>
 struct Cfg {
   static constexpr int TILE = D * 256;  // 128 rows x D x 2 B
-  static constexpr int NS = D == 64 ? 6 : 3;  // K/V ring stages
+  static constexpr int NS = D == 64 ? 10 : 5;  // K/V ring stages (P lives in TMEM)
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = Q_OFF + NT * TILE;
-  static constexpr int P_OFF = KV_OFF + NS * TILE;
-  static constexpr int BAR_OFF = P_OFF + NT * P_BYTES;
-  static constexpr int NBAR = 1 + 2 * NS + 4 * NT + 1;
+  static constexpr int BAR_OFF = KV_OFF + NS * TILE;
+  static constexpr int NBAR = 1 + 2 * NS + 3 * NT + 1;
   static constexpr size_t SMEM = 1024 + BAR_OFF + NBAR * 8 + 16;
   static_assert(SMEM <= kSmemLimit, "shared memory budget");
   static constexpr int O_COL = NT * BN;  // O_t at column O_COL + t * D
@@ -91,6 +93,25 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, 
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(da), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// D += A . B with A (M = 128 x K = 16, bf16 pairs packed per 32-bit column) in TMEM.
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]),
+      "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]),
+      "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -154,8 +175,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* kv_full = q_full + 1;    // [NS]
   uint64_t* kv_empty = kv_full + NS; // [NS]
   uint64_t* s_full = kv_empty + NS;  // [NT]
-  uint64_t* s_empty = s_full + NT;   // [NT]
-  uint64_t* p_full = s_empty + NT;   // [NT]
+  uint64_t* p_full = s_full + NT;    // [NT]: P_t(j) written over S_t(j) in TMEM
   uint64_t* p_empty = p_full + NT;   // [NT]: also "O_t holds P_t(j) V_j"
   uint64_t* done = p_empty + NT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -173,7 +193,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_empty[t], 4);
       mbar_init(&p_full[t], 4);
       mbar_init(&p_empty[t], 1);
     }
@@ -225,50 +244,52 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       constexpr uint32_t IDS = idesc_bf16(BN, false);
       constexpr uint32_t IDO = idesc_bf16(D, true);
-      // S_A(j), S_B(j) from K_j (ring item 2j); K_j's stage is freed after S_B(j).
-      auto issue_s = [&](int j) -> bool {
-        const int it = 2 * j, st = it % NS;
-        if (!mbar_wait(&kv_full[st], (it / NS) & 1, p.err, kDevErrFullWait)) return false;
-        const uint32_t k_base = smem_u32(smem + C::KV_OFF + st * C::TILE);
-        for (int t = 0; t < NT; ++t) {
-          if (!mbar_wait(&s_empty[t], (j & 1) ^ 1, p.err, kDevErrMmaWait)) return false;
-          tc_fence_after();
-          const uint32_t q_base = smem_u32(smem + C::Q_OFF + t * C::TILE);
+      // S_t(j) = Q_t K_j^T into TMEM columns [t*BN, t*BN + BN).
+      auto issue_s_tile = [&](int t, int j, uint32_t k_base) {
+        const uint32_t q_base = smem_u32(smem + C::Q_OFF + t * C::TILE);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
-            umma(tmem + t * BN, desc_k_sw128(q_base + off), desc_k_sw128(k_base + off), IDS, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[t]);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * ATOM + (kk & 3) * 32;
+          umma(tmem + t * BN, desc_k_sw128(q_base + off), desc_k_sw128(k_base + off), IDS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&kv_empty[st]);
-        return true;
-      };
-      // O_A += P_A(j) V_j, O_B += P_B(j) V_j (ring item 2j + 1, freed after both).
-      auto issue_pv = [&](int j) -> bool {
-        const int it = 2 * j + 1, st = it % NS;
-        if (!mbar_wait(&kv_full[st], (it / NS) & 1, p.err, kDevErrFullWait)) return false;
-        const uint32_t v_base = smem_u32(smem + C::KV_OFF + st * C::TILE);
-        for (int t = 0; t < NT; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, p.err, kDevErrMmaWait)) return false;
-          tc_fence_after();
-          const uint32_t p_base = smem_u32(smem + C::P_OFF + t * P_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t da = desc_k_sw128(p_base + (kk >> 2) * ATOM + (kk & 3) * 32);
-            const uint64_t db = desc_mn_sw128(v_base + kk * 2048, ATOM);
-            umma(tmem + C::O_COL + t * D, da, db, IDO, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&p_empty[t]);
-        }
-        umma_commit(&kv_empty[st]);
-        return true;
+        umma_commit(&s_full[t]);
       };
       if (!mbar_wait(q_full, 0, p.err, kDevErrFullWait)) ok = false;
-      if (ok && n > 0) ok = issue_s(0);
+      if (ok && n > 0) {
+        if (!mbar_wait(&kv_full[0], 0, p.err, kDevErrFullWait)) ok = false;
+        if (ok) {
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(smem + C::KV_OFF);
+          for (int t = 0; t < NT; ++t) issue_s_tile(t, 0, k_base);
+          umma_commit(&kv_empty[0]);
+        }
+      }
+      // Per j and tile: O_t += P_t(j) V_j (P from TMEM, where it overwrote
+      // S_t(j)), then S_t(j+1) into the same columns: the tensor pipe runs in
+      // issue order, so S_t(j+1) lands after P_t(j) has been read, and
+      // s_full_t(j+1) also tells the softmax that P_t(j) V_j is in O_t.
       for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n && !issue_s(j + 1)) ok = false;
-        if (ok && !issue_pv(j)) ok = false;
+        const int itv = 2 * j + 1, sv = itv % NS;
+        const int itk = 2 * j + 2, sk = itk % NS;
+        const bool more = j + 1 < n;
+        if (!mbar_wait(&kv_full[sv], (itv / NS) & 1, p.err, kDevErrFullWait)) { ok = false; break; }
+        if (more && !mbar_wait(&kv_full[sk], (itk / NS) & 1, p.err, kDevErrFullWait)) { ok = false; break; }
+        const uint32_t v_base = smem_u32(smem + C::KV_OFF + sv * C::TILE);
+        const uint32_t k_base = smem_u32(smem + C::KV_OFF + sk * C::TILE);
+        for (int t = 0; t < NT && ok; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, p.err, kDevErrMmaWait)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t db = desc_mn_sw128(v_base + kk * 2048, ATOM);
+            umma_ts(tmem + C::O_COL + t * D, tmem + t * BN + kk * 8, db, IDO, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&p_empty[t]);
+          if (more) issue_s_tile(t, j + 1, k_base);
+        }
+        if (!ok) break;
+        umma_commit(&kv_empty[sv]);
+        if (more) umma_commit(&kv_empty[sk]);
       }
     }
     __syncwarp();
@@ -285,8 +306,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int row = 32 * quarter + lane;
   const uint32_t tlane = tmem + ((uint32_t)(32 * quarter) << 16);
   const uint32_t s_col = t * BN, o_col = C::O_COL + t * D;
-  uint8_t* prow = smem + C::P_OFF + t * P_BYTES + row * 128;
-  const int sw = row & 7;
   float m_used = -INFINITY, l = 0.f;
   float s[BN];
   bool ok = true;
@@ -299,9 +318,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
     for (int c = 0; c < BN / 32; ++c) tmem_ld32(tlane + s_col + c * 32, s + c * 32);
     tmem_ld_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&s_empty[t]);
 
     const int valid = p.Lkv - j * BN;  // keys of this tile inside the sequence
     if (valid < BN) {                  // tail tile only (warp-uniform)
@@ -318,15 +334,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
       for (int u = 0; u < 4; ++u) mx4[u] = fmaxf(mx4[u], s[i + u]);
     const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
-    // P_t(j-1) V_{j-1} must be complete before O_t is rescaled or P_t is rewritten.
-    if (j > 0 && !mbar_wait(&p_empty[t], (j - 1) & 1, p.err, kDevErrMmaWait)) {
-      ok = false;
-      break;
-    }
     // New reference max only when some row's max grew past the threshold
     // (warp-uniform, since the O rescale below uses warp-collective tcgen05.ld/st).
-    // Rows whose max did not move get alpha = 1.
-    const bool rescale = __any_sync(0xffffffffu, mx > m_used + kRescaleThreshold);
+    // Rows whose max did not move get alpha = 1. P_t(j-1) V_{j-1} is already in
+    // O_t: it was issued before S_t(j), whose completion this warp waited for.
+    const bool grow = mx > m_used + kRescaleThreshold;
+    const bool rescale = __any_sync(0xffffffffu, grow);
     float alpha = 1.f;
     if (rescale) {
       const float m_new = fmaxf(m_used, mx);
@@ -334,29 +347,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       l *= alpha;
       m_used = m_new;
     }
-    // p = 2^(s * scale_log2 - m): one FFMA + ex2 per score, packed to bf16 and
-    // stored 8 at a time (the scores die as the loop advances); row sum as 4 chains.
+    // p = 2^(s * scale_log2 - m), packed to bf16 pairs and written over S_t in
+    // TMEM (64 columns), 64 scores at a time; row sum as 4 chains.
     const float neg_m = -m_used;
     float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < BN / 8; ++c) {
-      float e[8];
+    for (int h = 0; h < 2; ++h) {
+      uint32_t pk[32];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        e[u] = ex2(fmaf(s[8 * c + u], p.scale_log2, neg_m));
-        rs4[u & 3] += e[u];
+      for (int i = 0; i < 32; ++i) {
+        const float e0 = ex2(fmaf(s[64 * h + 2 * i], p.scale_log2, neg_m));
+        const float e1 = ex2(fmaf(s[64 * h + 2 * i + 1], p.scale_log2, neg_m));
+        rs4[i & 3] += e0 + e1;
+        pk[i] = pack_bf16x2(e0, e1);
       }
-      uint4 v;
-      v.x = pack_bf16x2(e[0], e[1]);
-      v.y = pack_bf16x2(e[2], e[3]);
-      v.z = pack_bf16x2(e[4], e[5]);
-      v.w = pack_bf16x2(e[6], e[7]);
-      *reinterpret_cast<uint4*>(prow + (c >> 3) * ATOM + (((c & 7) ^ sw) << 4)) = v;
+      tmem_st32u(tlane + s_col + 32 * h, pk);
+      tmem_st_wait();
     }
     l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-    // O_t *= alpha before P_t(j) V_j accumulates into it (the scores are dead here).
+    // O_t *= alpha before P_t(j) V_j accumulates into it.
     if (rescale && j > 0) {
-      tc_fence_after();
       float o[32];
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -368,7 +378,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       tmem_st_wait();
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&p_full[t]);
