@@ -413,7 +413,14 @@ def run_layer(args):
     lens = torch.full((Bl,), ctx, dtype=torch.int32, device=dev)
     gx = torch.Generator(device=dev).manual_seed(44)
     x = torch.randn(B, H, generator=gx, device=dev).to(torch.bfloat16)
-    if world > 1 and args.tp_mode == "peer":
+    dp = world > 1 and args.tp_mode == "dp"
+    if dp:
+        # Batch-parallel layer: every rank holds all weights and runs the whole
+        # step for its B/P sequences (their KV cache lives only there); no
+        # communication. x is this rank's rows of the global batch.
+        layer = DecodeLayer(full, HQ, HKV)
+        x = x[rank * Bl:(rank + 1) * Bl].contiguous()
+    elif world > 1 and args.tp_mode == "peer":
         layer = PeerTPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
     elif world > 1:
         layer = TPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
@@ -426,7 +433,7 @@ def run_layer(args):
         layer(x, k, v, lens)
     torch.cuda.synchronize()
     x_h = x.cpu().pin_memory()
-    y_h = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    y_h = torch.empty(x.shape[0], H, dtype=torch.bfloat16).pin_memory()
     x_d = torch.empty_like(x)
     step, step_e2e = (lambda: layer(x, k, v, lens)), None
 
@@ -488,20 +495,21 @@ def run_layer(args):
             "config": {"workload": "decode_layer_config5", "batch": B, "context": ctx, "hidden": H, "ffn": F,
                        "heads_q": HQ, "heads_kv": HKV,
                        "parallelism": "single GPU" if world == 1 else (
+                           f"dp{world}: batch-sharded layer, weights replicated, no collective" if dp else
                            f"tp{world} GEMMs + batch-sharded attention, all-gathers "
                            + ("in the GEMM / attention epilogues over peer memory" if args.tp_mode == "peer"
                               else "by NCCL")),
                        "cuda_graph": not args.no_graph,
                        "l2": "weights 436 MB + KV 4.3 GB per step exceed L2"},
-            "bytes_per_step": wbytes + kv_bytes,
-            "achieved_TBps": round((wbytes + kv_bytes) / world / (ms * 1e-3) / 1e12, 3),
+            "bytes_per_step": wbytes * (world if dp else 1) + kv_bytes,  # dp: every rank streams all weights
+            "achieved_TBps": round((wbytes * (world if dp else 1) + kv_bytes) / world / (ms * 1e-3) / 1e12, 3),
             "peak_GBps": peak, "peak_kind": kind,
             "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
             # this library's kernels per step: QKV (rms_split, GEMM, reduce; KV append
             # fused), attention (2), O-proj (GEMM, reduce), gate/up (rms_split, GEMM,
             # reduce), down (GEMM, reduce); under TP the append is its own kernel
-            "gpu_launches": args.steps * (12 if world == 1 else (18 if args.tp_mode == "peer" else 13)),
+            "gpu_launches": args.steps * (12 if (world == 1 or dp) else (18 if args.tp_mode == "peer" else 13)),
             "clocks": clk,
         }), flush=True)
     # Graphs that captured NCCL collectives must be freed before the process
@@ -526,8 +534,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="layer workload: launch eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--tp-mode", choices=["peer", "nccl"], default="peer",
-                    help="layer workload on N > 1 GPUs: all-gathers in the kernels over peer memory, or by NCCL")
+    ap.add_argument("--tp-mode", choices=["peer", "nccl", "dp"], default="peer",
+                    help="layer workload on N > 1 GPUs: tensor-parallel GEMMs with the all-gathers in the kernels "
+                         "over peer memory (peer) or by NCCL (nccl); or batch-parallel with replicated weights (dp)")
     ap.add_argument("--workload", choices=["attention", "layer"], default="attention",
                     help="attention: config 2 split-KV decode attention (headline); layer: config 5 decode step")
     args = ap.parse_args()
