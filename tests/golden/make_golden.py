@@ -10,7 +10,7 @@ such as ``@torch.compile`` dropped), executes them on the CPU in float64 on
 seeded bf16-representable inputs, and saves inputs + outputs as ``*.pt``.
 
 It runs only where the reference checkout exists (``--ref``, default
-``$FK_REFERENCE_DIR`` or ``/root/reference``); the fixtures it writes are
+``$FK_REFERENCE_DIR``); the fixtures it writes are
 committed so the tests never need the reference.
 
     python tests/golden/make_golden.py [--ref PATH]
@@ -198,8 +198,11 @@ def make_prefill(ref: Path, gen, B, H, Lq, Lkv, D, name):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--ref", default=os.environ.get("FK_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("FK_REFERENCE_DIR"),
+                    help="reference checkout (default: $FK_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.ref:
+        raise SystemExit("give --ref PATH or set FK_REFERENCE_DIR to the reference checkout")
     ref = Path(args.ref)
     if not (ref / "demo").is_dir():
         raise SystemExit(f"reference checkout not found at {ref}")
