@@ -3,6 +3,7 @@ functions take torch tensors directly, as the reference's compiled kernels do
 (README.md:1, python/cdsl_helpers/cdsl_fn_utils.py:38-44).
 
 Functions: ``dec_attn_splitkv_fwd``, ``dec_attn_combine``, ``dattn1``,
+``prefill_attn`` (FlashSM90's ``(mQ, mK, mV, mO, softmax_scale)``),
 ``skinny_gemm``, ``rmsnorm_linear``, ``swiglu_gemm``, ``swiglu_gemm2``,
 ``lora_gemm`` (the LoRA kernel's ``(a, b, lora_xA, lora_B, c)`` plus workspace),
 ``linear_workspace_bytes`` (same arguments and meaning as the C ABI in

@@ -81,6 +81,16 @@ void dattn1(TensorView Q, TensorView K, TensorView V, TensorView O, double softm
                   (int)K.size(1), (int)Q.size(2), stream_of(Q)));
 }
 
+// Prefill attention with FlashSM90's call shape (mQ, mK, mV, mO, softmax_scale):
+// [b, h, seqlen, d] tensors, d 64 or 128, k/v may have fewer heads than q.
+void prefill_attn(TensorView q, TensorView k, TensorView v, TensorView o, double softmax_scale) {
+  require(q.ndim() == 4 && k.ndim() == 4 && v.ndim() == 4 && o.ndim() == 4, "tensors must be [b, h, seqlen, d]");
+  use(q);
+  check(fk_prefill_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), nullptr, (int)q.size(0),
+                            (int)q.size(1), (int)k.size(1), (int)q.size(2), (int)k.size(2), (int)q.size(3),
+                            (float)softmax_scale, stream_of(q)));
+}
+
 // ---- linear family (x [M, K], w [N, K], y [M, N]; workspace zero-filled) ---
 void skinny_gemm(TensorView x, TensorView w, TensorView y, TensorView workspace) {
   use(x);
@@ -127,6 +137,7 @@ int64_t linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t swiglu) 
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_splitkv_fwd, dec_attn_splitkv_fwd);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_combine, dec_attn_combine);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(dattn1, dattn1);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(prefill_attn, prefill_attn);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(skinny_gemm, skinny_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(rmsnorm_linear, rmsnorm_linear);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm, swiglu_gemm);

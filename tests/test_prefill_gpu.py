@@ -115,3 +115,16 @@ def test_argument_errors():
     q3 = torch.zeros(1, 3, 64, 64, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):
         flash_attention(q3, k, v)  # 3 q heads over 2 kv heads
+
+
+def test_tvm_ffi_prefill_matches_ctypes():
+    """The TVM-FFI export (FlashSM90's call shape, torch tensors in) gives the ctypes path's result."""
+    pytest.importorskip("tvm_ffi")
+    from fused_kernels_cutedsl_lib_b200 import tvm_ffi_module
+
+    mod = tvm_ffi_module.load()
+    q, k, v = _inputs(1, 4, 2, 200, 300, 128, seed=9)
+    o = torch.empty_like(q)
+    mod.prefill_attn(q, k, v, o, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert torch.equal(o, flash_attention(q, k, v))
