@@ -4,6 +4,7 @@ functions take torch tensors directly, as the reference's compiled kernels do
 
 Functions: ``dec_attn_splitkv_fwd``, ``dec_attn_combine``, ``dattn1``,
 ``prefill_attn`` (FlashSM90's ``(mQ, mK, mV, mO, softmax_scale)``),
+``dattn2`` (DAttn2's call plus ``tmp`` [3, M, H*D] and workspace),
 ``skinny_gemm``, ``rmsnorm_linear``, ``swiglu_gemm``, ``swiglu_gemm2``,
 ``lora_gemm`` (the LoRA kernel's ``(a, b, lora_xA, lora_B, c)`` plus workspace),
 ``linear_workspace_bytes`` (same arguments and meaning as the C ABI in

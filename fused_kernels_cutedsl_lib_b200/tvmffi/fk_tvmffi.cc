@@ -91,6 +91,30 @@ void prefill_attn(TensorView q, TensorView k, TensorView v, TensorView o, double
                             (float)softmax_scale, stream_of(q)));
 }
 
+// DAttn2's call (X, Wq, Wk, Wv, Q_out, K_cache, V_cache) plus caller scratch:
+// tmp [3, M, H*D] bf16 for the three projections and a linear-family workspace.
+// Q_out [H, M, D] gets the head-major queries, K/V_cache [H, P, D] the new rows
+// at [P - M, P) (decoding_attention/attempt2.py:77-99, 276-286).
+void dattn2(TensorView x, TensorView wq, TensorView wk, TensorView wv, TensorView q_out, TensorView k_cache,
+            TensorView v_cache, TensorView tmp, TensorView workspace) {
+  require(x.ndim() == 2 && q_out.ndim() == 3 && k_cache.ndim() == 3 && v_cache.ndim() == 3 && tmp.ndim() == 3,
+          "X [M, H*D], Q_out [H, M, D], caches [H, P, D], tmp [3, M, H*D]");
+  use(x);
+  const int M = (int)x.size(0), HD = (int)x.size(1);
+  const int H = (int)q_out.size(0), D = (int)q_out.size(2), P = (int)k_cache.size(1);
+  require(H * D == HD && (int)q_out.size(1) == M, "Q_out must be [H, M, D] with H * D = X's features");
+  require((int)tmp.size(0) == 3 && (int)tmp.size(1) == M && (int)tmp.size(2) == HD, "tmp must be [3, M, H*D]");
+  void* st = stream_of(x);
+  char* t = static_cast<char*>(tmp.data_ptr());
+  const size_t plane = (size_t)M * HD * 2;
+  const TensorView* ws[3] = {&wq, &wk, &wv};
+  for (int i = 0; i < 3; ++i)
+    check(fk_skinny_gemm(x.data_ptr(), ws[i]->data_ptr(), t + i * plane, M, HD, HD, workspace.data_ptr(),
+                         nbytes(workspace), st));
+  check(fk_qkv_head_scatter(t, t + plane, t + 2 * plane, q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), M,
+                            H, D, P, st));
+}
+
 // ---- linear family (x [M, K], w [N, K], y [M, N]; workspace zero-filled) ---
 void skinny_gemm(TensorView x, TensorView w, TensorView y, TensorView workspace) {
   use(x);
@@ -138,6 +162,7 @@ TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_splitkv_fwd, dec_attn_splitkv_fwd);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_combine, dec_attn_combine);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(dattn1, dattn1);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(prefill_attn, prefill_attn);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(dattn2, dattn2);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(skinny_gemm, skinny_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(rmsnorm_linear, rmsnorm_linear);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm, swiglu_gemm);

@@ -281,3 +281,30 @@ def test_paged_kv_cache_matches_contiguous(block_size):
         assert torch.equal(got, qkv[b, Hq * 128:(Hq + Hkv) * 128])
         assert torch.equal(v_pool[blk, pos % block_size].reshape(-1), qkv[b, (Hq + Hkv) * 128:])
     assert lens_d.cpu().tolist() == (before + 1).tolist()
+
+
+def test_tvm_ffi_dattn2_matches_python_class():
+    """The TVM-FFI ``dattn2`` export (DAttn2's call plus scratch) equals the Python DAttn2 bit for bit."""
+    pytest.importorskip("tvm_ffi")
+    from fused_kernels_cutedsl_lib_b200 import DAttn2, alloc_workspace, tvm_ffi_module, workspace_bytes
+
+    mod = tvm_ffi_module.load()
+    torch.manual_seed(7)
+    M, H, D, P = 8, 8, 128, 96
+    X = torch.randn(M, H * D, device="cuda").bfloat16()
+    Ws = [(torch.randn(H * D, H * D, device="cuda") * 0.02).bfloat16() for _ in range(3)]
+    outs = []
+    for use_tvm in (False, True):
+        Q_out = torch.zeros(H, M, D, dtype=torch.bfloat16, device="cuda")
+        Kc = torch.zeros(H, P, D, dtype=torch.bfloat16, device="cuda")
+        Vc = torch.zeros(H, P, D, dtype=torch.bfloat16, device="cuda")
+        if use_tvm:
+            tmp = torch.empty(3, M, H * D, dtype=torch.bfloat16, device="cuda")
+            ws = alloc_workspace(workspace_bytes(M, H * D, H * D), "cuda")
+            mod.dattn2(X, *Ws, Q_out, Kc, Vc, tmp, ws)
+        else:
+            DAttn2()(X, *Ws, Q_out, Kc, Vc)
+        torch.cuda.synchronize()
+        outs.append((Q_out, Kc, Vc))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
