@@ -306,6 +306,7 @@ def run_ours(args):
             "pass_ms": {"splitkv_fwd": round(p1_ms, 5), "combine": round(p2_ms, 5)},
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved_gbs / peak, 4), "peak_kind": peak_kind,
+                         "frac_of_nominal_8000": round(achieved_gbs / 8000.0, 4),
                          "kernel": "splitkv_fwd_kernel",
                          "traffic": NCU_TRAFFIC_BYTES_PER_LAUNCH},
             "e2e": {"value": round(total_kv_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
