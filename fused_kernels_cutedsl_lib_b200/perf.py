@@ -155,6 +155,44 @@ def gemm_sweep(iters: int = 30, include_cublas: bool = True) -> list[dict]:
     return rows
 
 
+def attention_sweep(iters: int = 30) -> list[dict]:
+    """Decode attention (both passes) at configs 1 and 2: µs per call isolated and
+    back to back, KV-read TB/s and the fraction of the measured copy peak.
+    Config 1's 67 MB cache fits in L2, so it rotates over copies (> 300 MB) and
+    every call reads HBM; config 2's 17 GB padded cache needs none."""
+    from .decoding_attention import alloc_partials, dec_attn_splitkv_fwd, default_num_splits
+
+    peak = measured_peaks()
+    rows = []
+    for cfg in (configs.ATTN_CONFIG1, configs.ATTN_CONFIG2):
+        q, k, v, lens = configs.attn_inputs(cfg)
+        B, L = cfg.batch, cfg.max_seqlen
+        kv_bytes = cfg.kv_bytes(lens.cpu())
+        copies = [(k, v)]
+        while len(copies) * kv_bytes < (300 << 20):
+            copies.append((k.clone(), v.clone()))
+        S = default_num_splits(B, cfg.num_heads_kv, L)
+        out = torch.empty(B, 1, cfg.num_heads_q, 128, dtype=torch.bfloat16, device="cuda")
+        lse = torch.empty(B, cfg.num_heads_q, device="cuda")
+        o_p, l_p = alloc_partials(B, cfg.num_heads_q, S, "cuda")
+
+        def call(i):
+            kk, vv = copies[i % len(copies)]
+            dec_attn_splitkv_fwd(q, kk, vv, lens, out, lse, o_p, l_p, S)
+
+        t = statistics.median(time_launches(call, iters=iters))
+        tb = time_back_to_back(call)
+        rows.append({"kernel": "decode_attention", "config": cfg.name, "batch": B, "max_seqlen": L,
+                     "num_splits": S, "kv_bytes": kv_bytes, "kv_copies": len(copies),
+                     "us_per_call": round(t * 1e3, 2), "TBps": round(kv_bytes / (t * 1e-3) / 1e12, 3),
+                     "hbm_frac": round(kv_bytes / (t * 1e-3) / 1e9 / peak["hbm_gbs"], 3),
+                     "us_back_to_back": round(tb * 1e3, 2),
+                     "hbm_frac_back_to_back": round(kv_bytes / (tb * 1e-3) / 1e9 / peak["hbm_gbs"], 3)})
+        del q, k, v, copies
+        torch.cuda.empty_cache()
+    return rows
+
+
 def prefill_sweep(iters: int = 20) -> list[dict]:
     """Prefill attention at the reference's FlashSM90 test size ([16, 16, 4096, D],
     attn/attempt6_epi_pipeline/tests.py:138-154), D = 64 and 128, against torch
@@ -193,10 +231,13 @@ def main():
 
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=30)
-    ap.add_argument("--only", choices=["gemm", "prefill"], default=None)
+    ap.add_argument("--only", choices=["gemm", "prefill", "attention"], default=None)
     args = ap.parse_args()
     if args.only in (None, "gemm"):
         for r in gemm_sweep(args.iters):
+            print(json.dumps(r), flush=True)
+    if args.only in (None, "attention"):
+        for r in attention_sweep(args.iters):
             print(json.dumps(r), flush=True)
     if args.only in (None, "prefill"):
         for r in prefill_sweep():
