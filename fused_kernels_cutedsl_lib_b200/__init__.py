@@ -25,6 +25,7 @@ from .decoding_attention import (
     DAttn1,
     DAttn2,
     DecodeAttention,
+    alloc_counters,
     alloc_partials,
     chunk_tokens,
     dec_attn_combine,
@@ -32,6 +33,8 @@ from .decoding_attention import (
     dec_attn_splitkv_partial,
     decode_attention,
     default_num_splits,
+    fused_partial_slots,
+    plan_attention,
 )
 
 __all__ = [
@@ -54,6 +57,7 @@ __all__ = [
     "DAttn1",
     "DAttn2",
     "DecodeAttention",
+    "alloc_counters",
     "alloc_partials",
     "chunk_tokens",
     "dec_attn_combine",
@@ -61,4 +65,6 @@ __all__ = [
     "dec_attn_splitkv_partial",
     "decode_attention",
     "default_num_splits",
+    "fused_partial_slots",
+    "plan_attention",
 ]

@@ -105,6 +105,13 @@ SIGNATURES: dict[str, tuple] = {
         _c_int,
         [_p, ctypes.c_longlong, _c_int, _c_int, _p, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _p],
     ),
+    "fk_set_wait_limit_ns": (_c_int, [ctypes.c_ulonglong]),
+    "fk_dec_attn_fwd_fused": (
+        _c_int,
+        [_p, ctypes.c_longlong, _p, _p, _p, _p, _p, _p, _p, _c_int, _p, _p, _p, _p, _c_int, _c_int, _c_int,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _p],
+    ),
+    "fk_debug_attn_withhold_tile": (_c_int, [_c_int]),
     "fk_rmsnorm_swiglu": (
         _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
 }

@@ -23,9 +23,10 @@ int cuda_fail(cudaError_t e, const char* what) {
   return kErrCuda;
 }
 
-// One error word per device: the module-scope variable below has one instance
-// on every device that loads this library.
-__device__ int g_fk_device_error = 0;
+// One error block per device: the module-scope variable below has one instance
+// on every device that loads this library. [0] is the error word kernels write;
+// [2..3] hold the wait bound in ns (0: the built-in 1 s), see wait_limit_ns.
+__device__ __align__(16) int g_fk_device_error[4] = {0, 0, 0, 0};
 
 static constexpr int kMaxDevices = 64;
 
@@ -112,6 +113,13 @@ int fk_get_device_error(int* code_out, int clear) {
     FK_CHECK_CUDA(cudaMemcpy(w, &z, sizeof(int), cudaMemcpyHostToDevice));
   }
   *code_out = v;
+  return fk::kOk;
+}
+
+int fk_set_wait_limit_ns(unsigned long long ns) {
+  int* w = fk::device_error_word();
+  if (!w) return fk::fail(fk::kErrCuda, "device error word unavailable");
+  FK_CHECK_CUDA(cudaMemcpy(w + 2, &ns, sizeof(ns), cudaMemcpyHostToDevice));
   return fk::kOk;
 }
 

@@ -76,6 +76,14 @@ enum DeviceError : int {
 // legitimate wait inside these kernels (microseconds), far below a watchdog.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
+// The device error block is four ints: [0] the error code, [1] spare,
+// [2..3] a uint64 wait bound in ns set from the host (0: kWaitLimitNs). Tests
+// shorten the bound to make a withheld pipeline stage time out quickly.
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* err) {
+  const uint64_t v = *reinterpret_cast<const volatile unsigned long long*>(err + 2);
+  return v ? v : kWaitLimitNs;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -123,12 +131,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  const uint64_t lim = wait_limit_ns(err);
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) break;
+    if (global_timer_ns() - t0 > lim) break;
   }
   record_device_error(err, code);
   return false;
+}
+
+// Bounded wait for a group of warps that must leave together: besides its own
+// time bound, the wait gives up as soon as any warp of the group has set the
+// shared abort flag, and a warp whose bound runs out sets it. Every warp of the
+// group therefore stops waiting within one bound of the first time-out, so
+// the group still meets at its next named barrier instead of hanging there.
+// Warp-uniform: call with all lanes of a warp.
+__device__ __forceinline__ bool mbar_wait_group(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  const uint64_t lim = wait_limit_ns(err);
+  bool ok = false;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) {
+      ok = true;
+      break;
+    }
+    if (*abort_flag) break;
+    if (global_timer_ns() - t0 > lim) {
+      record_device_error(err, code);
+      *abort_flag = 1;
+      break;
+    }
+  }
+  // Lanes may leave on different iterations; agree on one answer per warp.
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------------------

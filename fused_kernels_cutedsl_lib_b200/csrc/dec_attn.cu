@@ -24,6 +24,8 @@
 // LSE-weighted and writes bf16 O and fp32 LSE.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "fk_b200.h"
 
@@ -33,7 +35,8 @@ namespace attn {
 constexpr int D = 128;                     // head_dim
 constexpr int T = 64;                      // tokens per KV tile
 constexpr int NCW = 4;                     // consumer warps (16 tokens each)
-constexpr int NTHREADS = (NCW + 1) * 32;   // + one TMA producer warp
+constexpr int NTHREADS = (NCW + 2) * 32;   // + one TMA producer warp + one finisher warp
+constexpr int NF = 4;                      // finisher hand-off ring depth (units)
 constexpr int HALF_BYTES = T * 128;        // 64 tokens x 64 dims x 2 B
 constexpr int TILE_BYTES = 2 * HALF_BYTES; // K (or V) tile: 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;// K + V: 32 KB
@@ -49,6 +52,15 @@ struct Params {
   int* err;
   int B, Lmax, Hq, Hkv, G, chunk;
   float scale_log2;
+  // Single-launch form (counters != null): the last unit of each (row, kv head)
+  // to finish merges that pair's splits and writes out / lse itself.
+  int* counters;           // [B * Hkv], zero between calls (each finisher resets its entry)
+  __nv_bfloat16* out;      // [B, Hq, D]
+  float* lse;              // [B, Hq]
+  int* seqlens_commit;     // optional: receives cache_seqlens[b] once row b is done with it
+  OutPlace peers;          // optional copies of out rows in other GPUs' buffers
+  int nseg_cap;            // single-launch form: partial slots per pair (leading dim of o_part), >= 2
+  int withhold_tile;       // test hook: CTA 0's producer skips its n-th tile (-1: never)
 };
 
 __device__ __forceinline__ int seq_len(const Params& p, int b) {
@@ -83,14 +95,171 @@ struct Walker {
   }
 };
 
+// LSE-weighted merge of the n splits of one (row, q head) by one warp; lane owns
+// dims [4*lane, 4*lane+4). kFresh: the partials were written by this grid
+// (read through L2 with ld.global.cg, not the non-coherent path). Writes bf16 out
+// (and its peer copies) and the natural-log lse. The sums run in split order, so
+// both launch forms give the same bits.
+template <bool kFresh>
+__device__ __forceinline__ float ld_part(const float* p) {
+  return kFresh ? __ldcg(p) : __ldg(p);
+}
+template <bool kFresh>
+__device__ __forceinline__ float4 ld_part4(const float* p) {
+  return kFresh ? __ldcg(reinterpret_cast<const float4*>(p)) : __ldg(reinterpret_cast<const float4*>(p));
+}
+
+template <bool kFresh>
+__device__ __forceinline__ void combine_row(const float* o_part, const float* lse_part, size_t plane, size_t row,
+                                            int n, int lane, __nv_bfloat16* out, float* lse, const OutPlace& peers) {
+  constexpr int CH = 8;  // splits whose loads are in flight together
+  float ls[CH];
+  float4 v[CH];
+  auto load_chunk = [&](int s0) {
+#pragma unroll
+    for (int u = 0; u < CH; ++u) {
+      if (s0 + u < n) {
+        ls[u] = ld_part<kFresh>(lse_part + (s0 + u) * plane + row);
+        v[u] = ld_part4<kFresh>(o_part + ((s0 + u) * plane + row) * D + 4 * lane);
+      } else {
+        ls[u] = -INFINITY;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  // The max over the splits' LSEs (exact, order-free). Up to 8 splits it comes
+  // from the first chunk itself, so the whole merge is one round trip to L2.
+  float M = -INFINITY;
+  if (n <= CH) {
+    load_chunk(0);
+#pragma unroll
+    for (int u = 0; u < CH; ++u) M = fmaxf(M, ls[u]);
+  } else {
+    for (int s = lane; s < n; s += 32) M = fmaxf(M, ld_part<kFresh>(lse_part + s * plane + row));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float W = 0.f;
+  if (M != -INFINITY) {
+    // The weighted sum runs in split order whatever the chunking.
+    for (int s0 = 0; s0 < n; s0 += CH) {
+      if (n > CH) load_chunk(s0);
+#pragma unroll
+      for (int u = 0; u < CH; ++u) {
+        if (s0 + u < n) {
+          const float wgt = expf(ls[u] - M);
+          W += wgt;
+          acc.x += wgt * v[u].x;
+          acc.y += wgt * v[u].y;
+          acc.z += wgt * v[u].z;
+          acc.w += wgt * v[u].w;
+        }
+      }
+    }
+  }
+  const bool ok = W > 0.f;
+  const float inv = ok ? 1.f / W : 0.f;
+  uint2 packed;
+  packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  reinterpret_cast<uint2*>(out + row * D)[lane] = packed;
+#pragma unroll
+  for (int i = 0; i < kMaxPeers; ++i)  // the same rows in other GPUs' buffers (all-gather of a batch shard)
+    if (i < peers.npeers) reinterpret_cast<uint2*>(peers.peer_y[i] + row * D)[lane] = packed;
+  if (lane == 0) lse[row] = ok ? M + logf(W) : -INFINITY;
+}
+
 __device__ __forceinline__ uint32_t keep_mask(bool lo, bool hi) {
   return (lo ? 0x0000FFFFu : 0u) | (hi ? 0xFFFF0000u : 0u);
 }
 
-template <int STAGES>
-__global__ void __launch_bounds__(NTHREADS, 1)
-    splitkv_fwd_kernel(const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, Params p) {
+__device__ __forceinline__ int seq_tiles(const Params& p, int b) { return (seq_len(p, b) + T - 1) / T; }
+
+// A run of consecutive 64-token tiles [i0, i1) of one (row b, kv head h) that
+// one CTA processes; its partial goes to split slot `slot` of the pair's
+// `nseg` slots. `final_of_cta`: the CTA has no work after it.
+struct Seg {
+  int b, h, i0, i1, slot, nseg;
+  bool final_of_cta;
+};
+
+// Two-launch form: units (b, h, split of `chunk` tokens) dealt round-robin.
+struct ChunkIter {
+  Walker w;
+  long long u;
+  __device__ void init(const Params& p) {
+    w.init(p);
+    u = blockIdx.x;
+  }
+  __device__ bool next(const Params& p, Seg& sg) {
+    int b, h, s;
+    if (!w.locate(p, u, b, h, s)) return false;
+    const int tpc = p.chunk / T;
+    sg.b = b;
+    sg.h = h;
+    sg.i0 = s * tpc;
+    sg.i1 = min(sg.i0 + tpc, seq_tiles(p, b));
+    sg.slot = s;
+    sg.nseg = w.nb;
+    sg.final_of_cta = false;
+    u += gridDim.x;
+    return true;
+  }
+};
+
+// Single-launch form (stream-K over tiles): the (row, kv head, tile) order is
+// cut into `G` contiguous ranges of equal length; CTA c owns
+// [c*total/G, (c+1)*total/G). A range that crosses a pair boundary gives one
+// segment per pair, and a pair's segments come from consecutive CTAs, so the
+// segment of CTA c writes slot c - owner(first tile of the pair).
+struct StreamIter {
+  long long t, t_end, total;
+  int G, b, nt;
+  long long row_base;
+  __device__ long long start(int c) const { return (long long)c * total / G; }
+  __device__ int owner(long long x) const { return (int)(((x + 1) * (long long)G - 1) / total); }
+  __device__ void init(const Params& p, long long total_tiles, int g) {
+    total = total_tiles;
+    G = g;
+    const int c = blockIdx.x;
+    t = c < G ? start(c) : 0;
+    t_end = c < G ? start(c + 1) : 0;
+    b = 0;
+    row_base = 0;
+    nt = p.B > 0 ? seq_tiles(p, 0) : 0;
+  }
+  __device__ bool next(const Params& p, Seg& sg) {
+    if (t >= t_end) return false;
+    while (t >= row_base + (long long)p.Hkv * nt) {  // t < total, so a later row holds it
+      row_base += (long long)p.Hkv * nt;
+      ++b;
+      nt = seq_tiles(p, b);
+    }
+    const long long r = t - row_base;
+    const int h = (int)(r / nt);
+    const long long pb = row_base + (long long)h * nt;
+    const long long pe = pb + nt;
+    const long long se = t_end < pe ? t_end : pe;
+    sg.b = b;
+    sg.h = h;
+    sg.i0 = (int)(t - pb);
+    sg.i1 = (int)(se - pb);
+    sg.slot = (int)blockIdx.x - owner(pb);
+    sg.nseg = owner(pe - 1) - owner(pb) + 1;
+    sg.final_of_cta = (se == t_end);
+    t = se;
+    return true;
+  }
+};
+
+// Pass 1 (FUSED = false: chunked units, partials for pass 2) or the whole
+// attention in one launch (FUSED = true: stream-K segments merged in-kernel).
+// Two CTAs per SM (shared memory allows two): registers are capped to fit them.
+template <int STAGES, bool FUSED>
+__global__ void __launch_bounds__(NTHREADS, 2)
+    splitkv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, Params p) {
+  using Iter = typename std::conditional<FUSED, StreamIter, ChunkIter>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -100,6 +269,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   float* co = cl + NCW * 8;                                           // [NCW][G][D]
   uint64_t* full = reinterpret_cast<uint64_t*>(co + NCW * p.G * D);
   uint64_t* empty = full + STAGES;
+  uint64_t* fin_full = empty + STAGES;  // [NF] a segment's partial is written (one arrival per consumer warp)
+  uint64_t* fin_empty = fin_full + NF;  // [NF] the finisher is done with that hand-off slot
+  volatile int* s_abort = reinterpret_cast<volatile int*>(fin_empty + NF);  // a consumer wait ran out
+  volatile int* s_last = s_abort + 1;                                       // this CTA merges the pair
+  volatile long long* s_total = reinterpret_cast<volatile long long*>(s_abort + 2);  // tiles in the batch
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -109,45 +283,136 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NCW);
     }
+    for (int i = 0; i < NF; ++i) {
+      mbar_init(&fin_full[i], NCW);
+      mbar_init(&fin_empty[i], 1);
+    }
+    *s_abort = 0;
     fence_barrier_init();
   }
-  __syncthreads();
-
-  Walker w;
-  w.init(p);
-  // Pass 2 may be scheduled now; it waits for this grid's completion itself.
+  if (warp == NCW && lane == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  // Launched as a programmatic dependent: the set-up above overlapped the
+  // previous kernel's tail; nothing that kernel may write (q, lengths, appended
+  // K/V rows, partials it may still read) is touched before it has completed.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  Iter it;
+  if constexpr (FUSED) {
+    // Every CTA counts the batch's tiles (the same number everywhere) and picks
+    // the number of ranges so that no pair is cut into more segments than the
+    // partial buffer holds: ranges of >= ceil(max tiles per pair / (cap - 1)) tiles.
+    if (warp == 0) {
+      long long sum = 0;
+      for (int b = lane; b < p.B; b += 32) sum += seq_tiles(p, b);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (lane == 0) *s_total = sum * p.Hkv;
+    }
+    __syncthreads();
+    const long long total = *s_total;
+    const int ntmax = (p.Lmax + T - 1) / T;
+    const int qmin = (ntmax + p.nseg_cap - 2) / (p.nseg_cap - 1);
+    long long g = total / qmin;
+    if (g > (long long)gridDim.x) g = gridDim.x;
+    if (g < 1) g = 1;
+    it.init(p, total, total > 0 ? (int)g : 0);
+  } else {
+    __syncthreads();
+    it.init(p);
+  }
+
+  if (warp == NCW + 1) {
+    // ------------------------------ finisher ------------------------------
+    // Single-launch form only. Takes each handed-off segment's partial from the
+    // consumers, counts it in for its (row, kv head) and, when it completes the
+    // count, merges that pair's segments and writes out / lse, while the
+    // consumers go on with the next segment.
+    if constexpr (FUSED) {
+      // Rows with no keys have no segments: out = 0, lse = -inf.
+      for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
+        if (seq_len(p, b) != 0) continue;
+        const size_t row0 = (size_t)b * p.Hq;
+        for (int i = lane; i < p.Hq * D / 4; i += 32) {
+          const uint2 z = make_uint2(0u, 0u);
+          reinterpret_cast<uint2*>(p.out + row0 * D)[i] = z;
+#pragma unroll
+          for (int pi = 0; pi < kMaxPeers; ++pi)
+            if (pi < p.peers.npeers) reinterpret_cast<uint2*>(p.peers.peer_y[pi] + row0 * D)[i] = z;
+        }
+        for (int i = lane; i < p.Hq; i += 32) p.lse[row0 + i] = -INFINITY;
+        if (p.seqlens_commit && lane == 0) p.seqlens_commit[b] = __ldg(p.seqlens + b);
+      }
+      const size_t plane = (size_t)p.B * p.Hq;
+      int k = 0;
+      Seg sg;
+      while (it.next(p, sg)) {
+        if (sg.nseg == 1 || sg.final_of_cta) continue;  // the consumers finish those
+        const int slot = k % NF;
+        if (!mbar_wait(&fin_full[slot], (k / NF) & 1, p.err, kDevErrFullWait)) return;
+        int last = 0;
+        if (lane == 0) {
+          // Release the partial (the consumers' stores, ordered before this
+          // thread by the hand-off barrier) at GPU scope, then count it in.
+          __threadfence();
+          int* ctr = p.counters + (size_t)sg.b * p.Hkv + sg.h;
+          last = atomicAdd(ctr, 1) == sg.nseg - 1;
+          if (last) *ctr = 0;  // every segment is in: reset for the next call
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();  // acquire: the pair's other partials are visible
+          for (int hh = 0; hh < p.G; ++hh)
+            combine_row<true>(p.o_part, p.lse_part, plane, (size_t)sg.b * p.Hq + (size_t)sg.h * p.G + hh,
+                              sg.nseg, lane, p.out, p.lse, p.peers);
+          if (sg.h == 0 && lane == 0 && p.seqlens_commit) p.seqlens_commit[sg.b] = __ldg(p.seqlens + sg.b);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&fin_empty[slot]);
+        ++k;
+      }
+    }
+    return;
+  }
 
   if (warp == NCW) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
       const uint64_t pol = l2_policy_evict_first();
       int stage = 0;
       uint32_t phase = 0;
-      for (long long u = blockIdx.x;; u += gridDim.x) {
-        int b, h, s;
-        if (!w.locate(p, u, b, h, s)) break;
-        const int L = seq_len(p, b);
-        const int t0 = s * p.chunk;
-        const int t1 = min(t0 + p.chunk, L);
-        for (int t = t0; t < t1; t += T) {
+      int issued = 0;
+      const int withhold = blockIdx.x == 0 ? p.withhold_tile : -1;
+      Seg sg;
+      while (it.next(p, sg)) {
+        const int L = seq_len(p, sg.b);
+        const int t1 = min(sg.i1 * T, L);
+        for (int t = sg.i0 * T; t < t1; t += T) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kDevErrEmptyWait)) return;
+          if (issued++ == withhold) {  // test hook: this stage never fills
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t* kd = ring + stage * STAGE_BYTES;
           uint8_t* vd = kd + TILE_BYTES;
           // Contiguous cache: (token, row). Paged: (token within block, physical
           // block); a 64-token tile never crosses a block (block_size % 64 == 0).
-          int ct = t, cb = b;
+          int ct = t, cb = sg.b;
           if (p.block_table) {
-            cb = __ldg(p.block_table + (size_t)b * p.max_blocks + t / p.block_size);
+            cb = __ldg(p.block_table + (size_t)sg.b * p.max_blocks + t / p.block_size);
             ct = t % p.block_size;
           }
-          tma_load_4d(kd, &tmK, &full[stage], 0, h, ct, cb, pol);
-          tma_load_4d(kd + HALF_BYTES, &tmK, &full[stage], 64, h, ct, cb, pol);
-          tma_load_4d(vd, &tmV, &full[stage], 0, h, ct, cb, pol);
-          tma_load_4d(vd + HALF_BYTES, &tmV, &full[stage], 64, h, ct, cb, pol);
+          tma_load_4d(kd, &tmK, &full[stage], 0, sg.h, ct, cb, pol);
+          tma_load_4d(kd + HALF_BYTES, &tmK, &full[stage], 64, sg.h, ct, cb, pol);
+          tma_load_4d(vd, &tmV, &full[stage], 0, sg.h, ct, cb, pol);
+          tma_load_4d(vd + HALF_BYTES, &tmV, &full[stage], 64, sg.h, ct, cb, pol);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -167,14 +432,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const float NEG_INF = -INFINITY;
   const int G = p.G;
 
+  int kfin = 0;  // segments handed to the finisher so far
   int stage = 0;
   uint32_t phase = 0;
-  for (long long u = blockIdx.x;; u += gridDim.x) {
-    int b, h, s;
-    if (!w.locate(p, u, b, h, s)) break;
+  Seg sg;
+  while (it.next(p, sg)) {
+    const int b = sg.b, h = sg.h;
     const int L = seq_len(p, b);
-    const int t0 = s * p.chunk;
-    const int t1 = min(t0 + p.chunk, L);
+    const int t0 = sg.i0 * T;
+    const int t1 = min(sg.i1 * T, L);
 
     // Q^T as the B operand: column n = query head g of the group (zero if g >= G).
     uint32_t qf[8][2];
@@ -199,7 +465,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float l0 = 0.f, l1 = 0.f;          // this lane's share of the running sums
 
     for (int t = t0; t < t1; t += T) {
-      if (!mbar_wait(&full[stage], phase, p.err, kDevErrFullWait)) return;
+      // A time-out leaves the tile loop; all consumer warps then meet at the
+      // merge barrier below and return together.
+      if (!mbar_wait_group(&full[stage], phase, p.err, kDevErrFullWait, s_abort)) break;
       const uint32_t kb = smem_u32(ring + stage * STAGE_BYTES);
       const uint32_t vb = kb + TILE_BYTES;
 
@@ -285,7 +553,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
 
-    // ---- merge the four warps' softmax states and write the unit's partial ----
+    // ---- merge the four warps' softmax states and write the segment's result ----
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
       l0 += __shfl_xor_sync(0xffffffffu, l0, off);
@@ -311,9 +579,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
     named_bar_sync(1, NCW * 32);
+    if (*s_abort) return;  // uniform: no consumer warp writes the flag past the barrier above
+    // A pair with one segment needs no merge: in the single-launch form that
+    // segment writes out / lse directly (the same values pass 2 gives: the
+    // weight of a lone split is exactly 1).
+    const bool direct = FUSED && sg.nseg == 1;
     {
       const int d = threadIdx.x;  // 0..127
-      const size_t row0 = ((size_t)s * p.B + b) * p.Hq + (size_t)h * G;
+      const size_t row0 = ((size_t)sg.slot * p.B + b) * p.Hq + (size_t)h * G;
+      const size_t orow0 = (size_t)b * p.Hq + (size_t)h * G;
       for (int hh = 0; hh < G; ++hh) {
         float M = NEG_INF;
 #pragma unroll
@@ -328,11 +602,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
         }
         const bool ok = Lsum > 0.f;
-        p.o_part[(row0 + hh) * D + d] = ok ? acc / Lsum : 0.f;
-        if (d == 0) p.lse_part[row0 + hh] = ok ? (M + log2f(Lsum)) * 0.69314718055994531f : NEG_INF;
+        const float ov = ok ? acc / Lsum : 0.f;
+        const float lv = ok ? (M + log2f(Lsum)) * 0.69314718055994531f : NEG_INF;
+        if (direct) {
+          const __nv_bfloat16 bv = __float2bfloat16_rn(ov);
+          p.out[(orow0 + hh) * D + d] = bv;
+#pragma unroll
+          for (int pi = 0; pi < kMaxPeers; ++pi)
+            if (pi < p.peers.npeers) p.peers.peer_y[pi][(orow0 + hh) * D + d] = bv;
+          if (d == 0) p.lse[orow0 + hh] = lv;
+        } else {
+          p.o_part[(row0 + hh) * D + d] = ov;
+          if (d == 0) p.lse_part[row0 + hh] = lv;
+        }
+      }
+    }
+    if constexpr (FUSED) {
+      if (direct) {
+        if (h == 0 && threadIdx.x == 0 && p.seqlens_commit) p.seqlens_commit[b] = __ldg(p.seqlens + b);
+      } else if (sg.final_of_cta) {
+        // The CTA's last segment: nothing follows it, so the consumers finish
+        // it themselves, one q head per warp.
+        named_bar_sync(1, NCW * 32);  // every partial store of this segment is issued
+        if (threadIdx.x == 0) {
+          __threadfence();  // release them at GPU scope, then count the segment in
+          int* ctr = p.counters + (size_t)b * p.Hkv + h;
+          const int last = atomicAdd(ctr, 1) == sg.nseg - 1;
+          if (last) *ctr = 0;
+          *s_last = last;
+        }
+        named_bar_sync(1, NCW * 32);
+        if (*s_last) {
+          __threadfence();  // acquire: the pair's other partials are visible
+          for (int hh = warp; hh < G; hh += NCW)
+            combine_row<true>(p.o_part, p.lse_part, (size_t)p.B * p.Hq, (size_t)b * p.Hq + (size_t)h * G + hh,
+                              sg.nseg, lane, p.out, p.lse, p.peers);
+          if (h == 0 && threadIdx.x == 0 && p.seqlens_commit) p.seqlens_commit[b] = __ldg(p.seqlens + b);
+        }
+      } else {
+        // Hand the partial to the finisher warp; a consumer waits only when
+        // the ring of NF slots is full.
+        const int slot = kfin % NF;
+        if (kfin < NF || mbar_wait_group(&fin_empty[slot], ((kfin / NF) & 1) ^ 1, p.err, kDevErrEmptyWait,
+                                         s_abort)) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&fin_full[slot]);
+        }
+        ++kfin;
       }
     }
     named_bar_sync(1, NCW * 32);
+    if (*s_abort) return;  // a hand-off wait ran out: all consumer warps leave together
   }
 }
 
@@ -358,56 +678,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ 
   if (seqlens_commit && row == b * Hq && lane == 0) seqlens_commit[b] = Lraw;
   int L = min(max(Lraw, 0), Lmax);
   const int n = (L + chunk - 1) / chunk;
-  const size_t plane = (size_t)B * Hq;
-  float M = -INFINITY;
-  for (int s = lane; s < n; s += 32) M = fmaxf(M, __ldg(lse_part + s * plane + row));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float W = 0.f;
-  if (M != -INFINITY) {
-    // Four splits' loads in flight per iteration (the loop is latency-bound
-    // otherwise); the sum still runs in split order.
-    int s = 0;
-    for (; s + 4 <= n; s += 4) {
-      float ls[4];
-      float4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        ls[u] = __ldg(lse_part + (s + u) * plane + row);
-        v[u] = __ldg(reinterpret_cast<const float4*>(o_part + ((s + u) * plane + row) * D) + lane);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float wgt = expf(ls[u] - M);
-        W += wgt;
-        acc.x += wgt * v[u].x;
-        acc.y += wgt * v[u].y;
-        acc.z += wgt * v[u].z;
-        acc.w += wgt * v[u].w;
-      }
-    }
-    for (; s < n; ++s) {
-      const float ls = __ldg(lse_part + s * plane + row);
-      const float wgt = expf(ls - M);
-      const float4 v = __ldg(reinterpret_cast<const float4*>(o_part + (s * plane + row) * D) + lane);
-      W += wgt;
-      acc.x += wgt * v.x;
-      acc.y += wgt * v.y;
-      acc.z += wgt * v.z;
-      acc.w += wgt * v.w;
-    }
-  }
-  const bool ok = W > 0.f;
-  const float inv = ok ? 1.f / W : 0.f;
-  uint2 packed;
-  packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-  packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-  reinterpret_cast<uint2*>(out + (size_t)row * D)[lane] = packed;
-#pragma unroll
-  for (int i = 0; i < kMaxPeers; ++i)  // the same rows in other GPUs' buffers (all-gather of a batch shard)
-    if (i < peers.npeers) reinterpret_cast<uint2*>(peers.peer_y[i] + (size_t)row * D)[lane] = packed;
-  if (lane == 0) lse[row] = ok ? M + logf(W) : -INFINITY;
+  combine_row<false>(o_part, lse_part, (size_t)B * Hq, (size_t)row, n, lane, out, lse, peers);
 }
 
 static int chunk_tokens(int Lmax, int num_splits) {
@@ -418,25 +689,42 @@ static int chunk_tokens(int Lmax, int num_splits) {
 template <int STAGES>
 static size_t fwd_smem_bytes(int G) {
   return 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)(2 * NCW * 8 + NCW * G * D) * 4 +
-         2 * STAGES * 8;
+         2 * STAGES * 8 + 2 * NF * 8 + 16;
 }
 
-template <int STAGES>
+template <int STAGES, bool FUSED>
 static int launch_fwd(const CUtensorMap& tmK, const CUtensorMap& tmV, const Params& p,
                       cudaStream_t stream) {
-  auto kern = splitkv_fwd_kernel<STAGES>;
+  auto kern = splitkv_kernel<STAGES, FUSED>;
   const size_t smem = fwd_smem_bytes<STAGES>(p.G);
   FK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int occ = 0;
   FK_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, NTHREADS, smem));
   if (occ < 1) occ = 1;
-  // Upper bound on the number of units: every row at full length.
-  const long long max_units =
-      (long long)p.B * p.Hkv * ((p.Lmax + p.chunk - 1) / p.chunk);
   long long grid = (long long)num_sms() * occ;
-  if (grid > max_units) grid = max_units;
+  if (!FUSED) {
+    // Upper bound on the number of units: every row at full length.
+    const long long max_units = (long long)p.B * p.Hkv * ((p.Lmax + p.chunk - 1) / p.chunk);
+    if (grid > max_units) grid = max_units;
+  } else {
+    const long long max_tiles = (long long)p.B * p.Hkv * ((p.Lmax + T - 1) / T);
+    if (grid > max_tiles) grid = max_tiles;
+  }
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, NTHREADS, smem, stream>>>(tmK, tmV, p);
+  // Programmatic dependent launch: barrier set-up and descriptor prefetch
+  // overlap the previous kernel's tail (the kernel waits for it before
+  // touching memory that kernel may write).
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, tmK, tmV, p));
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
 }
@@ -468,13 +756,26 @@ int fk_dec_attn_chunk_tokens(int max_seqlen, int num_splits) {
   return attn::chunk_tokens(max_seqlen, num_splits);
 }
 
+// Test hook (fk_debug_attn_withhold_tile): tile index CTA 0's producer skips, -1 never.
+static int g_withhold_tile = -1;
+
+// What the single-launch form writes besides the partials (counters null: pass 1 only).
+struct FusedOut {
+  int* counters = nullptr;
+  void* out = nullptr;
+  float* lse = nullptr;
+  int32_t* seqlens_commit = nullptr;
+  OutPlace peers = {};
+};
+
 // Paged form when block_table != null: k_cache/v_cache are block pools
 // [num_blocks, block_size, Hkv, D] and max_seqlen = max_blocks * block_size.
 static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cache, const void* v_cache,
                             const int32_t* cache_seqlens, float* o_partial, float* lse_partial,
                             int batch, int max_seqlen, int num_heads_q, int num_heads_kv,
                             int head_dim, int num_splits, float softmax_scale, void* stream,
-                            const int32_t* block_table = nullptr, int block_size = 0, int num_blocks = 0) {
+                            const int32_t* block_table = nullptr, int block_size = 0, int num_blocks = 0,
+                            const FusedOut& fo = FusedOut{}) {
   FK_CHECK_ARG(q_stride >= (long long)num_heads_q * head_dim && q_stride % 8 == 0,
                "q row stride must be >= num_heads_q * head_dim and a multiple of 8");
   int rc = check_attn_args(q, k_cache, v_cache, cache_seqlens, batch, max_seqlen, num_heads_q,
@@ -502,6 +803,20 @@ static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cac
   p.G = num_heads_q / num_heads_kv;
   p.chunk = attn::chunk_tokens(max_seqlen, num_splits);
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.counters = fo.counters;
+  p.out = static_cast<__nv_bfloat16*>(fo.out);
+  p.lse = fo.lse;
+  p.seqlens_commit = fo.seqlens_commit;
+  p.peers = fo.peers;
+  p.withhold_tile = g_withhold_tile;
+  p.nseg_cap = num_splits;
+  if (fo.counters) {
+    FK_CHECK_ARG(num_splits >= 2, "single-launch attention needs room for >= 2 partial slots per pair");
+    FK_CHECK_ARG(fo.out && fo.lse, "null out / lse");
+    FK_CHECK_ARG(((uintptr_t)fo.out & 7) == 0, "out must be 8-byte aligned");
+    FK_CHECK_ARG(((uintptr_t)fo.counters & 3) == 0, "counters must be 4-byte aligned");
+    FK_CHECK_ARG(fo.seqlens_commit != (int32_t*)cache_seqlens, "seqlens_commit must not alias cache_seqlens");
+  }
 
   // K/V cache [B, Lmax, Hkv, 128] bf16 viewed as a 4-D tensor (dim, head, token, batch).
   CUtensorMap tmK, tmV;
@@ -518,8 +833,12 @@ static int splitkv_fwd_impl(const void* q, long long q_stride, const void* k_cac
                   strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (p.G <= 4) return attn::launch_fwd<3>(tmK, tmV, p, st);
-  return attn::launch_fwd<2>(tmK, tmV, p, st);
+  if (fo.counters) {
+    if (p.G <= 4) return attn::launch_fwd<3, true>(tmK, tmV, p, st);
+    return attn::launch_fwd<2, true>(tmK, tmV, p, st);
+  }
+  if (p.G <= 4) return attn::launch_fwd<3, false>(tmK, tmV, p, st);
+  return attn::launch_fwd<2, false>(tmK, tmV, p, st);
 }
 
 int fk_dec_attn_splitkv_fwd(const void* q, const void* k_cache, const void* v_cache,
@@ -631,6 +950,39 @@ int fk_dec_attn_fwd_commit(const void* q, long long q_batch_stride, const void* 
   if (rc) return rc;
   return combine_impl(o_partial, lse_partial, cache_seqlens, seqlens_commit, out, lse, batch, max_seqlen,
                       num_heads_q, head_dim, num_splits, stream);
+}
+
+int fk_dec_attn_fwd_fused(const void* q, long long q_batch_stride, const void* k_cache, const void* v_cache,
+                          const int32_t* block_table, const int32_t* cache_seqlens, int32_t* seqlens_commit,
+                          void* out, void* const* peer_out, int npeers, float* lse, float* o_partial,
+                          float* lse_partial, int32_t* counters, int batch, int max_seqlen, int block_size,
+                          int num_blocks, int num_heads_q, int num_heads_kv, int head_dim, int num_splits,
+                          float softmax_scale, void* stream) {
+  FK_CHECK_ARG(counters != nullptr, "counters is null");
+  FK_CHECK_ARG(npeers >= 0 && npeers <= kMaxPeers, "npeers must be in [0, 7]");
+  if (block_table) {
+    FK_CHECK_ARG(block_size >= 64 && block_size % 64 == 0, "block_size must be a positive multiple of 64");
+    FK_CHECK_ARG(max_seqlen % block_size == 0 && num_blocks >= 1,
+                 "paged cache: max_seqlen must be max_blocks_per_seq * block_size, num_blocks >= 1");
+  }
+  FusedOut fo;
+  fo.counters = counters;
+  fo.out = out;
+  fo.lse = lse;
+  fo.seqlens_commit = seqlens_commit;
+  fo.peers.npeers = npeers;
+  for (int i = 0; i < npeers; ++i) {
+    FK_CHECK_ARG(peer_out && peer_out[i] && ((uintptr_t)peer_out[i] & 7) == 0, "peer output must be 8-byte aligned");
+    fo.peers.peer_y[i] = static_cast<__nv_bfloat16*>(peer_out[i]);
+  }
+  return splitkv_fwd_impl(q, q_batch_stride, k_cache, v_cache, cache_seqlens, o_partial, lse_partial, batch,
+                          max_seqlen, num_heads_q, num_heads_kv, head_dim, num_splits, softmax_scale, stream,
+                          block_table, block_size, num_blocks, fo);
+}
+
+int fk_debug_attn_withhold_tile(int tile) {
+  g_withhold_tile = tile < 0 ? -1 : tile;
+  return kOk;
 }
 
 int fk_dec_attn_fwd(const void* q, const void* k_cache, const void* v_cache,

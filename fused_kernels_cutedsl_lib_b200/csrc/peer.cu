@@ -50,13 +50,14 @@ __global__ void barrier_kernel(BarrierArgs a) {
     asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(a.peer_flags[r] + a.rank), "r"(seq) : "memory");
   }
   const uint64_t t0 = global_timer_ns();
+  const uint64_t lim = wait_limit_ns(a.err);
   for (int r = 0; r < a.nranks; ++r) {
     if (r == a.rank) continue;
     while (true) {
       int v;
       asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(a.local_flags + r) : "memory");
       if (v - seq >= 0) break;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > lim) {
         record_device_error(a.err, kDevErrFlagWait);
         return;
       }

@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* empty = full + STAGES;
   float* ss_sm = reinterpret_cast<float*>(empty + STAGES);  // [16]
   int* flag_sm = reinterpret_cast<int*>(ss_sm + 16);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(flag_sm + 1);  // a consumer wait ran out
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NCW);
     }
+    *s_abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
@@ -218,7 +220,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int t = 0; t < NT; ++t) ss[t] = 0.f;
 
     for (; it < seg_hi; ++it) {
-      if (!mbar_wait(&full[stage], phase, p.err, kDevErrFullWait)) return;
+      // A time-out leaves the k loop; every consumer warp then stops at the
+      // barrier after it and all return together.
+      if (!mbar_wait_group(&full[stage], phase, p.err, kDevErrFullWait, s_abort)) break;
       const uint8_t* st = smem + stage * LY::STAGE_BYTES;
       const uint32_t wb = smem_u32(st);
       const uint32_t xb = smem_u32(st + LY::X_OFF);
@@ -287,6 +291,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         phase ^= 1;
       }
     }
+
+    named_bar_sync(1, NCW * 32);
+    if (*s_abort) return;  // uniform: the flag is only written inside the k loop above
 
     // ------------------------- segment epilogue -------------------------
     float v[NMAT][NT][4];

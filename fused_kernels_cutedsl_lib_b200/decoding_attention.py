@@ -8,7 +8,11 @@ python/cdsl_helpers/cdsl_fn_utils.py:38-44). The callable writes the
 caller-allocated output in place and returns ``None``. This module keeps that
 ownership and calling style for the split-KV decode path:
 
-* :func:`dec_attn_splitkv_fwd` — both passes (the C ABI ``fk_dec_attn_fwd``);
+* :func:`dec_attn_splitkv_fwd` — the whole attention, either in ONE launch
+  (the C ABI ``fk_dec_attn_fwd_fused``: stream-K ranges of tiles, the last
+  piece of each (row, kv head) to finish merges the pair) or as two launches
+  (``fk_dec_attn_fwd``: fixed chunks, then pass 2); :func:`plan_attention`
+  picks the form by the batch's size;
 * :func:`dec_attn_splitkv_partial` / :func:`dec_attn_combine` — pass 1 / pass 2;
 * :class:`DecodeAttention` — a kernel object in the reference's style whose
   ``__call__(q, k_cache, v_cache, cache_seqlens, out, lse, softmax_scale)``
@@ -21,7 +25,9 @@ attn/attempt6_epi_pipeline/my_softmax.py:88-97 (a row with no keys yields 0).
 """
 from __future__ import annotations
 
+import ctypes
 import math
+import threading
 
 import torch
 
@@ -44,11 +50,20 @@ def default_num_splits(batch: int, num_heads_kv: int, max_seqlen: int,
     that still gives at least one work unit (row, kv head, split) per SM.
 
     Large chunks amortise each unit's setup (q load, pipeline fill) and keep
-    pass 2 short; at config 2's ~1.1 M tokens 1024-token chunks still give
-    ~8700 units, dealt round-robin. Measured at config 1 (B = 4, L = 4096):
-    4-8 splits take 18-19 us per call back to back, 64 splits (the earlier
-    "4 units per resident CTA" rule) 36.5 us. ``total_tokens`` (sum of the true
-    lengths) sharpens the count for ragged batches.
+    the merge of the splits short; at config 2's ~1.1 M tokens 1024-token
+    chunks still give ~8700 units, dealt round-robin. The pass-1 grid keeps two
+    CTAs resident per SM (shared memory allows two), so a count just above one
+    unit per SM leaves some resident CTAs idle; at config 1 (B = 4, L = 4096)
+    the rule gives 8 splits = 256 units for 296 resident CTAs, every unit
+    running in the first wave. Measured at config 1: 4-8 splits take 18-19 us
+    per call back to back (two-launch form), 64 splits (the earlier "4 units
+    per resident CTA" rule) 36.5 us; configs 1 and 2 are the measured shapes.
+
+    ``total_tokens`` (sum of the true lengths) sharpens the count for ragged
+    batches. Callers whose lengths live on the GPU (the decode layer) leave it
+    out: reading them would synchronise the host with the device every step,
+    so the padded count ``batch * max_seqlen`` stands in and can pick a larger
+    chunk than the true work supports.
     """
     total = total_tokens if total_tokens is not None else batch * max_seqlen
     chunk = TILE_TOKENS
@@ -58,6 +73,45 @@ def default_num_splits(batch: int, num_heads_kv: int, max_seqlen: int,
             chunk = c
             break
     return max(1, -(-max_seqlen // chunk))
+
+
+def fused_partial_slots(batch: int, num_heads_kv: int, max_seqlen: int, num_sms: int = 148) -> int:
+    """Partial slots per (row, kv head) for the single-launch form.
+
+    That form cuts the batch's (row, kv head, 64-token tile) sequence into one
+    equal range per resident CTA (two per SM) and merges the pieces of each pair
+    in-kernel; a pair cut into n pieces uses n partial slots. The kernel picks
+    ranges long enough that no pair needs more slots than the buffer holds, so
+    more slots let it keep every CTA busy on shorter (ragged) batches. This
+    sizes the buffer for a batch whose true tokens are down to a quarter of the
+    padded ``batch * max_seqlen``: ceil(tiles per row * CTAs * 4 / padded
+    tiles) + 1, within [2, tiles per row + 1].
+    """
+    ntmax = -(-max_seqlen // TILE_TOKENS)
+    grid = 2 * num_sms
+    padded = max(1, batch * num_heads_kv * ntmax)
+    slots = -(-(ntmax * grid * 4) // padded) + 1
+    return max(2, min(slots, ntmax + 1))
+
+
+# Padded tiles per resident CTA from which the single launch pays off. Below it
+# (config 1: B = 4, L = 4096 gives 7) the in-kernel merge's atomic and L2 round
+# trips at the end of the kernel cost more than pass 2 launched as a programmatic
+# dependent: measured 23.3 vs 21.5 us per call at config 1, while at config 2
+# (885 per CTA) the single launch is faster (674 vs 684-687 us).
+SINGLE_LAUNCH_MIN_TILES_PER_CTA = 32
+
+
+def plan_attention(batch: int, num_heads_kv: int, max_seqlen: int, num_sms: int = 148) -> tuple[bool, int]:
+    """(single_launch, num_splits) for a batch shape: the single-launch form with
+    :func:`fused_partial_slots` slots when the batch gives every resident CTA (two
+    per SM) at least ``SINGLE_LAUNCH_MIN_TILES_PER_CTA`` padded 64-token tiles,
+    else the two-launch form with :func:`default_num_splits` chunks."""
+    ntmax = -(-max_seqlen // TILE_TOKENS)
+    per_cta = batch * num_heads_kv * ntmax / (2 * num_sms)
+    if per_cta >= SINGLE_LAUNCH_MIN_TILES_PER_CTA:
+        return True, fused_partial_slots(batch, num_heads_kv, max_seqlen, num_sms)
+    return False, default_num_splits(batch, num_heads_kv, max_seqlen, num_sms=num_sms)
 
 
 def _check_attn(q, k_cache, v_cache, cache_seqlens):
@@ -135,9 +189,65 @@ def dec_attn_combine(o_partial, lse_partial, cache_seqlens, out, lse, max_seqlen
         B, int(max_seqlen), Hq, D, S, st))
 
 
+def alloc_counters(batch: int, num_heads_kv: int, device) -> torch.Tensor:
+    """Zeroed arrival counters of the single-launch form: one int32 per (row, kv head).
+    Every call leaves them zero again, so one buffer serves any number of calls
+    that are ordered on the GPU."""
+    return torch.zeros(batch * num_heads_kv, dtype=torch.int32, device=device)
+
+
+_ctr_lock = threading.Lock()
+_ctr_cache: dict = {}
+
+
+def shared_counters(n: int, device, stream_handle: int) -> torch.Tensor:
+    """Counters for callers that pass none: one zeroed buffer per (device, stream),
+    grown on demand. Calls on one stream are ordered, so they can share it; a
+    different stream gets its own buffer."""
+    key = (str(device), int(stream_handle))
+    with _ctr_lock:
+        buf = _ctr_cache.get(key)
+        if buf is None or buf.numel() < n:
+            buf = torch.zeros(max(n, 1024), dtype=torch.int32, device=device)
+            _ctr_cache[key] = buf
+        return buf
+
+
+def _vptrs(ptrs):
+    arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+    return arr, len(ptrs)
+
+
+def attn_fused_launch(q_ptr: int, q_batch_stride: int, k_cache, v_cache, cache_seqlens, out_ptr: int, lse,
+                      o_partial, lse_partial, counters, *, batch: int, max_seqlen: int, num_heads_q: int,
+                      num_heads_kv: int, num_splits: int, softmax_scale: float, stream_handle: int,
+                      block_table=None, block_size: int = 0, num_blocks: int = 0, seqlens_commit=None,
+                      peer_out=()) -> None:
+    """Raw call of ``fk_dec_attn_fwd_fused`` (pointers and sizes already checked by the caller)."""
+    peers, npeers = _vptrs(list(peer_out))
+    _native.check(_native.load().fk_dec_attn_fwd_fused(
+        q_ptr, q_batch_stride, ptr(k_cache), ptr(v_cache),
+        ptr(block_table) if block_table is not None else None, ptr(cache_seqlens),
+        ptr(seqlens_commit) if seqlens_commit is not None else None, out_ptr, peers, npeers, ptr(lse),
+        ptr(o_partial), ptr(lse_partial), ptr(counters), batch, max_seqlen, block_size, num_blocks,
+        num_heads_q, num_heads_kv, HEAD_DIM, num_splits, float(softmax_scale), stream_handle))
+
+
 def dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_partial, lse_partial,
-                         num_splits: int, softmax_scale: float | None = None, stream=None) -> None:
-    """Both passes: ``out = softmax(q K^T * scale) V`` per row over its first ``cache_seqlens[b]`` keys."""
+                         num_splits: int, softmax_scale: float | None = None, stream=None, *,
+                         counters=None, single_launch: bool | None = None) -> None:
+    """``out = softmax(q K^T * scale) V`` per row over its first ``cache_seqlens[b]`` keys.
+
+    ``single_launch`` (default): one kernel. Each CTA takes an equal range of
+    the batch's (row, kv head, 64-token tile) sequence; the last piece of each
+    (row, kv head) to finish merges the pair, through ``counters`` (int32
+    ``[B * Hkv]``, zero; :func:`alloc_counters`; default: a buffer shared per
+    device and stream). ``num_splits`` is then the number of partial slots per
+    pair the buffers hold (>= 2, see :func:`fused_partial_slots`).
+    ``single_launch=False``: pass 1 over ``num_splits`` fixed chunks, then pass 2.
+    ``single_launch=None`` (default): the form :func:`plan_attention` picks for
+    this shape (single launch needs ``num_splits >= 2``).
+    """
     B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
     _check_partials(o_partial, lse_partial, num_splits, B, Hq)
     require_tensor("out", out, torch.bfloat16)
@@ -148,55 +258,76 @@ def dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_partial
     same_device(q, out, lse, o_partial, lse_partial)
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     st = stream_for(dev, stream)
-    _native.check(_native.load().fk_dec_attn_fwd(
-        ptr(q), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), ptr(lse),
-        ptr(o_partial), ptr(lse_partial), B, L, Hq, Hkv, D, num_splits, scale, st))
+    if single_launch is None:
+        single_launch = num_splits >= 2 and plan_attention(B, Hkv, L)[0]
+    if not single_launch:
+        _native.check(_native.load().fk_dec_attn_fwd(
+            ptr(q), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), ptr(lse),
+            ptr(o_partial), ptr(lse_partial), B, L, Hq, Hkv, D, num_splits, scale, st))
+        return
+    if counters is None:
+        counters = shared_counters(B * Hkv, dev, st)
+    else:
+        require_tensor("counters", counters, torch.int32, 1)
+        if counters.numel() < B * Hkv:
+            raise ValueError(f"counters must hold >= {B * Hkv} entries, got {counters.numel()}")
+        same_device(q, counters)
+    attn_fused_launch(ptr(q), Hq * D, k_cache, v_cache, cache_seqlens, ptr(out), lse, o_partial, lse_partial,
+                      counters, batch=B, max_seqlen=L, num_heads_q=Hq, num_heads_kv=Hkv, num_splits=num_splits,
+                      softmax_scale=scale, stream_handle=st)
 
 
 class DecodeAttention:
     """Kernel object in the reference's style (cf. ``DAttn1(...)`` then a call).
 
     ``DecodeAttention(num_splits=None)(q, k_cache, v_cache, cache_seqlens, out, lse,
-    softmax_scale)`` runs both passes, writing ``out``/``lse`` in place and
-    returning ``None``. Split partials are allocated once per (shape, device)
-    and reused; pass ``num_splits`` to pin the split count, else
-    :func:`default_num_splits` picks it from the padded length.
+    softmax_scale)`` runs decode attention in the form :func:`plan_attention`
+    picks for the shape, writing ``out``/``lse`` in place and returning ``None``.
+    Partials and counters are allocated once per (shape, device) and reused;
+    ``num_splits`` pins the split count (two-launch) or partial slots (single launch).
     """
 
     def __init__(self, num_splits: int | None = None):
         self.num_splits = num_splits
         self._ws: dict = {}
 
-    def splits_for(self, batch: int, num_heads_kv: int, max_seqlen: int) -> int:
+    def plan(self, batch: int, num_heads_kv: int, max_seqlen: int) -> tuple[bool, int]:
+        single, S = plan_attention(batch, num_heads_kv, max_seqlen)
         if self.num_splits is not None:
-            return int(self.num_splits)
-        return default_num_splits(batch, num_heads_kv, max_seqlen)
+            S = int(self.num_splits)
+            single = single and S >= 2
+        return single, S
 
-    def workspace(self, batch, num_heads_q, num_splits, device):
-        key = (batch, num_heads_q, num_splits, str(device))
+    def workspace(self, batch, num_heads_q, num_heads_kv, num_splits, device):
+        key = (batch, num_heads_q, num_heads_kv, num_splits, str(device))
         ws = self._ws.get(key)
         if ws is None:
-            ws = alloc_partials(batch, num_heads_q, num_splits, device)
+            ws = alloc_partials(batch, num_heads_q, num_splits, device) + (
+                alloc_counters(batch, num_heads_kv, device),)
             self._ws[key] = ws
         return ws
 
     def __call__(self, q, k_cache, v_cache, cache_seqlens, out, lse, softmax_scale=None,
                  stream=None) -> None:
         B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
-        S = self.splits_for(B, Hkv, L)
-        o_p, l_p = self.workspace(B, Hq, S, dev)
+        single, S = self.plan(B, Hkv, L)
+        o_p, l_p, ctr = self.workspace(B, Hq, Hkv, S, dev)
         dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S,
-                             softmax_scale, stream)
+                             softmax_scale, stream, counters=ctr, single_launch=single)
 
 
 def decode_attention(q, k_cache, v_cache, cache_seqlens, softmax_scale=None, num_splits=None):
     """Functional convenience: allocates ``out``/``lse``/partials, returns ``(out, lse)``."""
     B, L, Hq, Hkv, D, dev = _check_attn(q, k_cache, v_cache, cache_seqlens)
-    S = num_splits if num_splits is not None else default_num_splits(B, Hkv, L)
+    single, S = plan_attention(B, Hkv, L)
+    if num_splits is not None:
+        S = num_splits
+        single = single and S >= 2
     out = torch.empty((B, 1, Hq, D), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((B, Hq), dtype=torch.float32, device=dev)
     o_p, l_p = alloc_partials(B, Hq, S, dev)
-    dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, softmax_scale)
+    dec_attn_splitkv_fwd(q, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, softmax_scale,
+                         single_launch=single)
     return out, lse
 
 
@@ -279,7 +410,8 @@ class DAttn2:
 
 
 def dec_attn_paged_fwd(q, k_pool, v_pool, block_table, cache_seqlens, out, lse, o_partial, lse_partial,
-                       num_splits: int, softmax_scale: float | None = None, stream=None) -> None:
+                       num_splits: int, softmax_scale: float | None = None, stream=None, *,
+                       single_launch: bool | None = None) -> None:
     """Split-KV decode attention over a paged KV cache (both passes).
 
     ``k_pool``/``v_pool``: [num_blocks, block_size, Hkv, 128] bf16 with
@@ -306,6 +438,15 @@ def dec_attn_paged_fwd(q, k_pool, v_pool, block_table, cache_seqlens, out, lse, 
     dev = same_device(q, k_pool, v_pool, block_table, cache_seqlens, out, lse, o_partial, lse_partial)
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
     st = stream_for(dev, stream)
-    _native.check(_native.load().fk_dec_attn_fwd_paged(
-        ptr(q), ptr(k_pool), ptr(v_pool), ptr(block_table), ptr(cache_seqlens), ptr(out), ptr(lse),
-        ptr(o_partial), ptr(lse_partial), B, MB, BS, NB, Hq, Hkv, D, num_splits, scale, st))
+    if single_launch is None:
+        single_launch = num_splits >= 2 and plan_attention(B, Hkv, MB * BS)[0]
+    if not single_launch:
+        _native.check(_native.load().fk_dec_attn_fwd_paged(
+            ptr(q), ptr(k_pool), ptr(v_pool), ptr(block_table), ptr(cache_seqlens), ptr(out), ptr(lse),
+            ptr(o_partial), ptr(lse_partial), B, MB, BS, NB, Hq, Hkv, D, num_splits, scale, st))
+        return
+    counters = shared_counters(B * Hkv, dev, st)
+    attn_fused_launch(ptr(q), Hq * D, k_pool, v_pool, cache_seqlens, ptr(out), lse, o_partial, lse_partial,
+                      counters, batch=B, max_seqlen=MB * BS, num_heads_q=Hq, num_heads_kv=Hkv,
+                      num_splits=num_splits, softmax_scale=scale, stream_handle=st, block_table=block_table,
+                      block_size=BS, num_blocks=NB)

@@ -9,9 +9,9 @@ One step for a batch of B sequences, each generating one token:
 5. ``gu = silu(g) * u`` for ``[g; u] = rms_norm(h, gamma_ffn) @ W_gu^T``   fused RMSNorm->gate/up->SwiGLU
 6. ``y = h + gu @ W_down^T``                         GEMM with residual epilogue
 
-Twelve kernel launches (tcgen05 path: RMSNorm prologue, GEMM and split-row-block
-reduction per RMSNorm GEMM, GEMM and reduction per plain GEMM, two attention
-passes), no host synchronisation and no torch compute on the path.
+Eleven kernel launches (tcgen05 path: RMSNorm prologue, GEMM and split-row-block
+reduction per RMSNorm GEMM, GEMM and reduction per plain GEMM, one single-launch
+attention), no host synchronisation and no torch compute on the path.
 The reference has no layer composition; this follows the decode path's full
 layer configuration (hidden 4096, 32 q / 8 kv heads of 128, FFN 14336).
 
@@ -21,7 +21,7 @@ features) with an NCCL all-gather of each GEMM's output, and attention is
 batch-parallel (each rank holds the KV cache of B/P rows), its output
 all-gathered over rows. :class:`PeerTPDecodeLayer` computes the same step with
 the all-gathers done by the kernels themselves: each GEMM epilogue and
-attention's pass 2 store their output blocks into every rank's buffer over
+attention's merge store their output blocks into every rank's buffer over
 peer memory, with a stage barrier kernel between stages.
 """
 from __future__ import annotations
@@ -34,7 +34,8 @@ import torch
 
 from . import _native
 from ._tensors import ptr, stream_for
-from .decoding_attention import alloc_partials, default_num_splits
+from .decoding_attention import (alloc_counters, alloc_partials, attn_fused_launch, plan_attention,
+                                 shared_counters)
 from .gemm import alloc_workspace, linear, workspace_bytes, workspace_for
 from .sharding import column_range, shard_gate_up
 
@@ -98,14 +99,22 @@ def kv_append_paged(qkv, k_pool, v_pool, block_table, cache_seqlens, num_heads_q
 
 
 def attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_partial, lse_partial, num_splits,
-                       num_heads_q, num_heads_kv, softmax_scale=None, stream=None):
+                       num_heads_q, num_heads_kv, softmax_scale=None, stream=None, counters=None,
+                       single_launch=True):
     """Split-KV attention reading q from the first ``Hq*128`` columns of each ``qkv`` row."""
     B, L = k_cache.shape[0], k_cache.shape[1]
     scale = 1.0 / math.sqrt(HEAD_DIM) if softmax_scale is None else float(softmax_scale)
     st = stream_for(qkv.device, stream)
-    _native.check(_native.load().fk_dec_attn_fwd_ex(
-        ptr(qkv), qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), ptr(lse),
-        ptr(o_partial), ptr(lse_partial), B, L, num_heads_q, num_heads_kv, HEAD_DIM, num_splits, scale, st))
+    if not single_launch:
+        _native.check(_native.load().fk_dec_attn_fwd_ex(
+            ptr(qkv), qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens), ptr(out), ptr(lse),
+            ptr(o_partial), ptr(lse_partial), B, L, num_heads_q, num_heads_kv, HEAD_DIM, num_splits, scale, st))
+        return
+    if counters is None:
+        counters = shared_counters(B * num_heads_kv, qkv.device, st)
+    attn_fused_launch(ptr(qkv), qkv.stride(0), k_cache, v_cache, cache_seqlens, ptr(out), lse, o_partial,
+                      lse_partial, counters, batch=B, max_seqlen=L, num_heads_q=num_heads_q,
+                      num_heads_kv=num_heads_kv, num_splits=num_splits, softmax_scale=scale, stream_handle=st)
 
 
 def linear_kv_append(x, w, out, k_cache, v_cache, cache_seqlens, seqlens_next, num_heads_q, num_heads_kv, *,
@@ -137,9 +146,11 @@ def linear_kv_append(x, w, out, k_cache, v_cache, cache_seqlens, seqlens_next, n
 
 
 def attention_commit(qkv, k_cache, v_cache, cache_seqlens, seqlens_commit, out, lse, o_partial, lse_partial,
-                     num_splits, num_heads_q, num_heads_kv, *, block_table=None, softmax_scale=None, stream=None):
+                     num_splits, num_heads_q, num_heads_kv, *, block_table=None, softmax_scale=None, stream=None,
+                     counters=None, single_launch=True):
     """:func:`attention_from_qkv` that also copies the lengths it used into
-    ``seqlens_commit`` (pass 2 writes them; a different tensor from ``cache_seqlens``)."""
+    ``seqlens_commit`` (a different tensor from ``cache_seqlens``), written by
+    the unit that finishes each row (``single_launch``) or by pass 2."""
     B = qkv.shape[0]
     if block_table is not None:
         bs = k_cache.shape[1]
@@ -148,10 +159,19 @@ def attention_commit(qkv, k_cache, v_cache, cache_seqlens, seqlens_commit, out, 
         L, bs, nblk = k_cache.shape[1], 0, 0
     scale = 1.0 / math.sqrt(HEAD_DIM) if softmax_scale is None else float(softmax_scale)
     st = stream_for(qkv.device, stream)
-    _native.check(_native.load().fk_dec_attn_fwd_commit(
-        ptr(qkv), qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(block_table) if block_table is not None else None,
-        ptr(cache_seqlens), ptr(seqlens_commit), ptr(out), ptr(lse), ptr(o_partial), ptr(lse_partial), B, L, bs,
-        nblk, num_heads_q, num_heads_kv, HEAD_DIM, num_splits, scale, st))
+    if not single_launch:
+        _native.check(_native.load().fk_dec_attn_fwd_commit(
+            ptr(qkv), qkv.stride(0), ptr(k_cache), ptr(v_cache),
+            ptr(block_table) if block_table is not None else None, ptr(cache_seqlens), ptr(seqlens_commit),
+            ptr(out), ptr(lse), ptr(o_partial), ptr(lse_partial), B, L, bs, nblk, num_heads_q, num_heads_kv,
+            HEAD_DIM, num_splits, scale, st))
+        return
+    if counters is None:
+        counters = shared_counters(B * num_heads_kv, qkv.device, st)
+    attn_fused_launch(ptr(qkv), qkv.stride(0), k_cache, v_cache, cache_seqlens, ptr(out), lse, o_partial,
+                      lse_partial, counters, batch=B, max_seqlen=L, num_heads_q=num_heads_q,
+                      num_heads_kv=num_heads_kv, num_splits=num_splits, softmax_scale=scale, stream_handle=st,
+                      block_table=block_table, block_size=bs, num_blocks=nblk, seqlens_commit=seqlens_commit)
 
 
 class DecodeLayer:
@@ -178,13 +198,17 @@ class DecodeLayer:
         key = (B, L, str(device))
         b = self._bufs.get(key)
         if b is None:
-            S = self.num_splits or default_num_splits(B, self.hkv, L)
+            single, S = plan_attention(B, self.hkv, L)
+            if self.num_splits:
+                S = self.num_splits
+                single = single and S >= 2
             o_p, l_p = alloc_partials(B, self.hq, S, device)
             ws = max(workspace_bytes(B, n, k, sw) for n, k, sw in [
                 (self.qkv_dim, self.hidden, False), (self.hidden, self.hq * HEAD_DIM, False),
                 (self.ffn, self.hidden, True), (self.hidden, self.ffn, False)])
             bf = dict(dtype=torch.bfloat16, device=device)
-            b = dict(S=S, o_p=o_p, l_p=l_p, ws=alloc_workspace(ws, device),
+            b = dict(S=S, single=single, o_p=o_p, l_p=l_p, ws=alloc_workspace(ws, device),
+                     ctr=alloc_counters(B, self.hkv, device),
                      qkv=torch.empty(B, self.qkv_dim, **bf), attn=torch.empty(B, self.hq * HEAD_DIM, **bf),
                      lse=torch.empty(B, self.hq, dtype=torch.float32, device=device),
                      h=torch.empty(B, self.hidden, **bf), gu=torch.empty(B, self.ffn, **bf),
@@ -203,12 +227,14 @@ class DecodeLayer:
             linear_kv_append(x, w.w_qkv, b["qkv"], k_cache, v_cache, cache_seqlens, b["lens_next"], self.hq,
                              self.hkv, gamma=w.gamma_attn, eps=self.eps, workspace=ws, stream=stream)
             attention_commit(b["qkv"], k_cache, v_cache, b["lens_next"], cache_seqlens, b["attn"], b["lse"],
-                             b["o_p"], b["l_p"], b["S"], self.hq, self.hkv, stream=stream)
+                             b["o_p"], b["l_p"], b["S"], self.hq, self.hkv, stream=stream, counters=b["ctr"],
+                             single_launch=b["single"])
         else:
             linear(x, w.w_qkv, b["qkv"], gamma=w.gamma_attn, eps=self.eps, workspace=ws, stream=stream)
             kv_append(b["qkv"], k_cache, v_cache, cache_seqlens, self.hq, self.hkv, stream=stream)
             attention_from_qkv(b["qkv"], k_cache, v_cache, cache_seqlens, b["attn"], b["lse"], b["o_p"], b["l_p"],
-                               b["S"], self.hq, self.hkv, stream=stream)
+                               b["S"], self.hq, self.hkv, stream=stream, counters=b["ctr"],
+                               single_launch=b["single"])
         linear(b["attn"], w.w_o, b["h"], residual=x, workspace=ws, stream=stream)
         linear(b["h"], w.w_gate_up, b["gu"], gamma=w.gamma_ffn, eps=self.eps, w_up=w.w_gate_up,
                up_row_offset=self.ffn, workspace=ws, stream=stream)
@@ -251,11 +277,12 @@ class KernelOps:
 
     def append_and_attend(self, qkv, k_cache, v_cache, cache_seqlens, out):
         B, L = k_cache.shape[0], k_cache.shape[1]
-        S = default_num_splits(B, self.hkv, L)
+        single, S = plan_attention(B, self.hkv, L)
         o_p, l_p = alloc_partials(B, self.hq, S, qkv.device)
         lse = torch.empty(B, self.hq, dtype=torch.float32, device=qkv.device)
         kv_append(qkv, k_cache, v_cache, cache_seqlens, self.hq, self.hkv)
-        attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, self.hq, self.hkv)
+        attention_from_qkv(qkv, k_cache, v_cache, cache_seqlens, out, lse, o_p, l_p, S, self.hq, self.hkv,
+                           single_launch=single)
         return out
 
 
@@ -369,14 +396,16 @@ class PeerTPDecodeLayer:
         if self.arena is None:
             self.arena = PeerArena(2 * B * (self.n_qkv + self.hq * HEAD_DIM + 2 * H + F) + (1 << 16), self.group)
         a = self.arena
-        S = default_num_splits(Bl, self.hkv, L)
+        single, S = plan_attention(Bl, self.hkv, L)
         o_p, l_p = alloc_partials(Bl, self.hq, S, device)
         ws_need = max(workspace_bytes(B, n, k, sw) for n, k, sw in [
             (self.w.w_qkv.shape[0], H, False), (self.w.w_o.shape[0], self.hq * HEAD_DIM, False),
             (self.w.w_gate_up.shape[0] // 2, H, True), (self.w.w_down.shape[0], F, False)])
         b = dict(qkv=a.region(f"qkv{B}", (B, self.n_qkv)), attn=a.region(f"attn{B}", (B, self.hq * HEAD_DIM)),
                  h=a.region(f"h{B}", (B, H)), gu=a.region(f"gu{B}", (B, F)), y=a.region(f"y{B}", (B, H)),
-                 S=S, o_p=o_p, l_p=l_p, lse=torch.empty(Bl, self.hq, dtype=torch.float32, device=device),
+                 S=S, single=single, o_p=o_p, l_p=l_p,
+                 lse=torch.empty(Bl, self.hq, dtype=torch.float32, device=device),
+                 ctr=alloc_counters(Bl, self.hkv, device),
                  ws=alloc_workspace(ws_need, device))
         self._bufs[key] = b
         return b
@@ -410,12 +439,18 @@ class PeerTPDecodeLayer:
         my_qkv = b["qkv"][r0:r0 + Bl]
         kv_append(my_qkv, k_cache, v_cache, cache_seqlens, self.hq, self.hkv)
         hd = self.hq * HEAD_DIM
-        peers, n = _vp(a.peer_ptrs("attn" + B_, r0 * hd))
-        scale = 1.0 / math.sqrt(HEAD_DIM)
-        _native.check(_native.load().fk_dec_attn_fwd_peers(
-            ptr(my_qkv), my_qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens),
-            b["attn"].data_ptr() + 2 * r0 * hd, peers, n, ptr(b["lse"]), ptr(b["o_p"]), ptr(b["l_p"]), Bl, L,
-            self.hq, self.hkv, HEAD_DIM, b["S"], scale, ctypes.c_void_p(st)))
+        if b["single"]:
+            attn_fused_launch(ptr(my_qkv), my_qkv.stride(0), k_cache, v_cache, cache_seqlens,
+                              b["attn"].data_ptr() + 2 * r0 * hd, b["lse"], b["o_p"], b["l_p"], b["ctr"], batch=Bl,
+                              max_seqlen=L, num_heads_q=self.hq, num_heads_kv=self.hkv, num_splits=b["S"],
+                              softmax_scale=1.0 / math.sqrt(HEAD_DIM), stream_handle=st,
+                              peer_out=a.peer_ptrs("attn" + B_, r0 * hd))
+        else:
+            peers, n = _vp(a.peer_ptrs("attn" + B_, r0 * hd))
+            _native.check(_native.load().fk_dec_attn_fwd_peers(
+                ptr(my_qkv), my_qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens),
+                b["attn"].data_ptr() + 2 * r0 * hd, peers, n, ptr(b["lse"]), ptr(b["o_p"]), ptr(b["l_p"]), Bl, L,
+                self.hq, self.hkv, HEAD_DIM, b["S"], 1.0 / math.sqrt(HEAD_DIM), ctypes.c_void_p(st)))
         a.barrier()
         # O-projection + residual x
         self._linear(b["attn"], w.w_o, b["h"], "h" + B_, self.c_lo, H, b, residual=x.data_ptr() + 2 * self.c_lo,

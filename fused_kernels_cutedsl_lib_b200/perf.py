@@ -155,12 +155,14 @@ def gemm_sweep(iters: int = 30, include_cublas: bool = True) -> list[dict]:
     return rows
 
 
-def attention_sweep(iters: int = 30) -> list[dict]:
-    """Decode attention (both passes) at configs 1 and 2: µs per call isolated and
-    back to back, KV-read TB/s and the fraction of the measured copy peak.
+def attention_sweep(iters: int = 30, splits_sweep: bool = True) -> list[dict]:
+    """Decode attention at configs 1 and 2, single-launch and two-launch forms: µs
+    per call isolated and back to back, KV-read TB/s and the fraction of the
+    measured copy peak.
     Config 1's 67 MB cache fits in L2, so it rotates over copies (> 300 MB) and
     every call reads HBM; config 2's 17 GB padded cache needs none."""
-    from .decoding_attention import alloc_partials, dec_attn_splitkv_fwd, default_num_splits
+    from .decoding_attention import (alloc_counters, alloc_partials, dec_attn_splitkv_fwd, default_num_splits,
+                                     fused_partial_slots)
 
     peak = measured_peaks()
     rows = []
@@ -171,23 +173,29 @@ def attention_sweep(iters: int = 30) -> list[dict]:
         copies = [(k, v)]
         while len(copies) * kv_bytes < (300 << 20):
             copies.append((k.clone(), v.clone()))
-        S = default_num_splits(B, cfg.num_heads_kv, L)
-        out = torch.empty(B, 1, cfg.num_heads_q, 128, dtype=torch.bfloat16, device="cuda")
-        lse = torch.empty(B, cfg.num_heads_q, device="cuda")
-        o_p, l_p = alloc_partials(B, cfg.num_heads_q, S, "cuda")
+        S0 = default_num_splits(B, cfg.num_heads_kv, L)
+        ctr = alloc_counters(B, cfg.num_heads_kv, "cuda")
+        variants = [(fused_partial_slots(B, cfg.num_heads_kv, L), True), (S0, False)]
+        if cfg is configs.ATTN_CONFIG1 and splits_sweep:
+            variants += [(s, True) for s in (5, 9, 17)] + [(s, False) for s in (4, 16) if s != S0]
+        for S, single in variants:
+            out = torch.empty(B, 1, cfg.num_heads_q, 128, dtype=torch.bfloat16, device="cuda")
+            lse = torch.empty(B, cfg.num_heads_q, device="cuda")
+            o_p, l_p = alloc_partials(B, cfg.num_heads_q, S, "cuda")
 
-        def call(i):
-            kk, vv = copies[i % len(copies)]
-            dec_attn_splitkv_fwd(q, kk, vv, lens, out, lse, o_p, l_p, S)
+            def call(i):
+                kk, vv = copies[i % len(copies)]
+                dec_attn_splitkv_fwd(q, kk, vv, lens, out, lse, o_p, l_p, S, single_launch=single, counters=ctr)
 
-        t = statistics.median(time_launches(call, iters=iters))
-        tb = time_back_to_back(call)
-        rows.append({"kernel": "decode_attention", "config": cfg.name, "batch": B, "max_seqlen": L,
-                     "num_splits": S, "kv_bytes": kv_bytes, "kv_copies": len(copies),
-                     "us_per_call": round(t * 1e3, 2), "TBps": round(kv_bytes / (t * 1e-3) / 1e12, 3),
-                     "hbm_frac": round(kv_bytes / (t * 1e-3) / 1e9 / peak["hbm_gbs"], 3),
-                     "us_back_to_back": round(tb * 1e3, 2),
-                     "hbm_frac_back_to_back": round(kv_bytes / (tb * 1e-3) / 1e9 / peak["hbm_gbs"], 3)})
+            t = statistics.median(time_launches(call, iters=iters))
+            tb = time_back_to_back(call)
+            rows.append({"kernel": "decode_attention", "config": cfg.name, "batch": B, "max_seqlen": L,
+                         "num_splits": S, "launches": 1 if single else 2, "kv_bytes": kv_bytes,
+                         "kv_copies": len(copies),
+                         "us_per_call": round(t * 1e3, 2), "TBps": round(kv_bytes / (t * 1e-3) / 1e12, 3),
+                         "hbm_frac": round(kv_bytes / (t * 1e-3) / 1e9 / peak["hbm_gbs"], 3),
+                         "us_back_to_back": round(tb * 1e3, 2),
+                         "hbm_frac_back_to_back": round(kv_bytes / (tb * 1e-3) / 1e9 / peak["hbm_gbs"], 3)})
         del q, k, v, copies
         torch.cuda.empty_cache()
     return rows
@@ -246,3 +254,110 @@ def main():
 
 if __name__ == "__main__":
     main()
+
+
+# ---------------------------------------------------------------------------
+# Sub-benchmarks of bench.py's JSON line (the reference project's benchmark list
+# beyond the headline): each returns plain numbers; bench.py adds the roofline
+# denominators and the CPU baselines.
+# ---------------------------------------------------------------------------
+
+def launch_floor(iters: int = 30) -> dict:
+    """Device time of a one-element torch kernel timed like every number here:
+    what any single launch costs on this pool before it moves a byte."""
+    x = torch.zeros(1, device="cuda")
+    t = statistics.median(time_launches(lambda i: x.add_(1), iters=iters))
+    tb = time_back_to_back(lambda i: x.add_(1))
+    return {"us_isolated": round(t * 1e3, 2), "us_back_to_back": round(tb * 1e3, 2)}
+
+
+def bench_attention_config1(iters: int = 30) -> dict:
+    """Config 1 (B=4, L=4096, 32q/8kv, 67 MB of KV) through the default entry point
+    (the form plan_attention picks). The cache rotates over copies (> 300 MB) so
+    every call reads HBM."""
+    from .decoding_attention import alloc_counters, alloc_partials, dec_attn_splitkv_fwd, plan_attention
+
+    cfg = configs.ATTN_CONFIG1
+    q, k, v, lens = configs.attn_inputs(cfg)
+    B, L = cfg.batch, cfg.max_seqlen
+    kv_bytes = cfg.kv_bytes(lens.cpu())
+    copies = [(k, v)]
+    while len(copies) * kv_bytes < (300 << 20):
+        copies.append((k.clone(), v.clone()))
+    single, S = plan_attention(B, cfg.num_heads_kv, L)
+    out = torch.empty(B, 1, cfg.num_heads_q, 128, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, cfg.num_heads_q, device="cuda")
+    o_p, l_p = alloc_partials(B, cfg.num_heads_q, S, "cuda")
+    ctr = alloc_counters(B, cfg.num_heads_kv, "cuda")
+
+    def call(i):
+        kk, vv = copies[i % len(copies)]
+        dec_attn_splitkv_fwd(q, kk, vv, lens, out, lse, o_p, l_p, S, single_launch=single, counters=ctr)
+
+    t = statistics.median(time_launches(call, iters=iters))
+    tb = time_back_to_back(call)
+    return {"kv_bytes": kv_bytes, "algorithmic_bytes": kv_bytes + cfg.io_bytes(),
+            "form": "single launch" if single else "two launches (pass 2 as a programmatic dependent)",
+            "num_splits": S, "kv_copies": len(copies), "launches_per_call": 1 if single else 2,
+            "us_isolated": round(t * 1e3, 2), "us_back_to_back": round(tb * 1e3, 2)}
+
+
+def bench_linear_shard(kind: str, M: int, N: int, K: int, seed: int, rank: int = 0, world: int = 1,
+                       iters: int = 30, include_cublas: bool = True) -> dict:
+    """One rank's column shard of a config-3 / config-4 GEMM (``world`` = 1: the whole GEMM).
+
+    kind: "plain" (y = x W^T, config 3), "rmsnorm" (RMSNorm -> W_qkv, config 4a) or
+    "swiglu" (RMSNorm-free gate/up + SwiGLU on W [2N, K], config 4b: gate and up
+    rows of the same columns stay on one rank). Weights rotate over copies so
+    every launch streams HBM. Returns µs per launch isolated and back to back and
+    the shard's algorithmic bytes."""
+    from .sharding import column_range, shard_gate_up
+
+    sw = kind == "swiglu"
+    x, w = configs.gemm_inputs(M, 2 * N if sw else N, K, seed)
+    if world > 1:
+        if sw:
+            w = shard_gate_up(w, rank, world)
+        else:
+            lo, hi = column_range(N, rank, world)
+            w = w[lo:hi].contiguous()
+    n_local = w.shape[0] // 2 if sw else w.shape[0]
+    gamma = None
+    if kind == "rmsnorm":
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        gamma = (1 + 0.1 * torch.randn(K, generator=g, device="cuda")).bfloat16()
+    y = torch.empty(M, n_local, dtype=torch.bfloat16, device="cuda")
+    ws = alloc_workspace(workspace_bytes(M, n_local, K, sw), "cuda")
+    wl = weight_copies(w)
+    nw = len(wl)
+
+    def ours(i):
+        wi = wl[i % nw]
+        if sw:
+            linear(x, wi, y, w_up=wi, up_row_offset=n_local, workspace=ws)
+        else:
+            linear(x, wi, y, gamma=gamma, eps=1e-6, workspace=ws)
+
+    t = statistics.median(time_launches(ours, iters))
+    tb = time_back_to_back(ours)
+    nbytes = w.numel() * 2 + M * K * 2 + M * n_local * 2 + (K * 2 if gamma is not None else 0)
+    row = {"M": M, "N": N, "K": K, "N_local": n_local, "bytes_local": nbytes,
+           "flops_local": 2 * M * w.shape[0] * K,
+           "path": "stream-K mma.sync (M <= 16)" if M <= 16 else "tcgen05 / TMEM",
+           "us_isolated": round(t * 1e3, 2), "us_back_to_back": round(tb * 1e3, 2), "weight_copies": nw}
+    if include_cublas:
+        if sw:
+            def ref(i):
+                o = x @ wl[i % nw].t()
+                torch.nn.functional.silu(o[:, :n_local]) * o[:, n_local:]
+        elif gamma is not None:
+            def ref(i):
+                torch.nn.functional.rms_norm(x, (K,), weight=gamma, eps=1e-6) @ wl[i % nw].t()
+        else:
+            def ref(i):
+                x @ wl[i % nw].t()
+        row["torch_us_isolated"] = round(statistics.median(time_launches(ref, iters)) * 1e3, 2)
+        row["torch_us_back_to_back"] = round(time_back_to_back(ref) * 1e3, 2)
+    del wl, w, x, y, ws
+    torch.cuda.empty_cache()
+    return row

@@ -52,6 +52,10 @@ FK_API int fk_use_device(int device);
  * 0 = no error, 1/2 = a pipeline stage wait ran out, 3 = a tensor-core commit
  * wait ran out, 4 = a global-flag wait ran out. Synchronous. */
 FK_API int fk_get_device_error(int* code_out, int clear);
+/* Sets the bound on every device-side wait of this library's kernels on the
+ * current device, in ns (0 restores the built-in 1 s). Synchronous. Tests
+ * shorten it so that a deliberately starved pipeline times out quickly. */
+FK_API int fk_set_wait_limit_ns(unsigned long long ns);
 
 /* ---- split-KV decode attention ------------------------------------------
  * Replaces the reference's decode attention kernel DAttn1
@@ -131,6 +135,35 @@ FK_API int fk_dec_attn_fwd_commit(const void* q, long long q_batch_stride, const
                                   float* lse_partial, int batch, int max_seqlen, int block_size, int num_blocks,
                                   int num_heads_q, int num_heads_kv, int head_dim, int num_splits,
                                   float softmax_scale, void* stream);
+
+/* Single-launch decode attention: pass 2 folded into pass 1. Every unit
+ * (row, kv head, split) writes its partial; the last unit of a (row, kv head)
+ * to finish, found by an atomic count per pair, merges that pair's splits in
+ * split order and writes out / lse (the same bits as fk_dec_attn_fwd). Rows
+ * with one split write out / lse directly and touch no partials. No unit waits
+ * on another. Covers every variant of the two-pass entries: q at a row stride
+ * (q_batch_stride, elements); a paged cache when block_table is non-null
+ * (max_seqlen = max_blocks_per_seq * block_size); seqlens_commit (optional,
+ * receives cache_seqlens[b] once row b is done); npeers <= 7 copies of each
+ * out row at peer_out[i] (other GPUs' buffers, same offsets).
+ *   counters  [batch * num_heads_kv] int32, zero before the first call; each
+ *             call leaves them zero again. Calls that may overlap on the GPU
+ *             need their own counters.
+ * Replaces the reference's decode-attention pair dec_attn_run /
+ * dec_attn_second_part (demo/dec_attn_run.py:45-46,
+ * demo/dec_attn_second_part.py:17-43) in one launch. */
+FK_API int fk_dec_attn_fwd_fused(const void* q, long long q_batch_stride, const void* k_cache,
+                                 const void* v_cache, const int32_t* block_table, const int32_t* cache_seqlens,
+                                 int32_t* seqlens_commit, void* out, void* const* peer_out, int npeers, float* lse,
+                                 float* o_partial, float* lse_partial, int32_t* counters, int batch,
+                                 int max_seqlen, int block_size, int num_blocks, int num_heads_q,
+                                 int num_heads_kv, int head_dim, int num_splits, float softmax_scale,
+                                 void* stream);
+
+/* Test hook: CTA 0 of every later decode-attention launch skips issuing its
+ * tile number `tile` (a stage that never fills), so its consumers' bounded
+ * waits run out; -1 turns it off. Host-side setting, no GPU work. */
+FK_API int fk_debug_attn_withhold_tile(int tile);
 
 /* Paged form of fk_kv_append: the new row of b goes to block
  * block_table[b][len / block_size], row len % block_size (any block_size >= 1). */

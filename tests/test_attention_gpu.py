@@ -49,7 +49,8 @@ def run(q, k, v, lens, num_splits, scale=None):
     o_p, l_p = alloc_partials(B, Hq, num_splits, q.device)
     o_p.fill_(float("nan"))
     l_p.fill_(float("nan"))
-    dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, num_splits, scale)
+    # the two-launch form: pass 1 over num_splits fixed chunks, pass 2
+    dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, num_splits, scale, single_launch=False)
     torch.cuda.synchronize()
     assert _native.device_error() == 0
     return out, lse
