@@ -150,6 +150,112 @@ void lora_gemm(TensorView x, TensorView w, TensorView lora_xa, TensorView lora_b
                        nbytes(workspace), stream_of(x)));
 }
 
+// ---- reference call shapes without a workspace argument ---------------------
+// The reference's compiled kernels take only their operands (Gemm4SM90(...)(a, b, c),
+// Swiglu2SM90(...)(a, b, b1, c)); their split-K scratch lives here instead: one
+// zeroed buffer per device from fk_peer_alloc, grown when a call needs more and
+// kept until exit. Every call leaves the buffer's counters zero again, so
+// calls ordered on one stream share it; calls on concurrent streams must use
+// the explicit-workspace functions.
+void* module_workspace(int device, size_t need, size_t* have) {
+  static void* bufs[64] = {};
+  static size_t sizes[64] = {};
+  require(device >= 0 && device < 64, "device index out of range");
+  if (sizes[device] < need) {
+    if (bufs[device]) check(fk_peer_free(bufs[device]));
+    bufs[device] = nullptr;
+    sizes[device] = 0;
+    void* p = nullptr;
+    const size_t n = need < ((size_t)16 << 20) ? ((size_t)16 << 20) : need;
+    check(fk_peer_alloc(n, &p));
+    bufs[device] = p;
+    sizes[device] = n;
+  }
+  *have = sizes[device];
+  return bufs[device];
+}
+
+void gemm(TensorView a, TensorView b, TensorView c) {
+  use(a);
+  const int M = (int)a.size(0), N = (int)b.size(0), K = (int)a.size(1);
+  size_t need = 0, have = 0;
+  check(fk_linear_workspace_bytes(M, N, K, 0, &need));
+  void* ws = module_workspace(a.device().device_id, need, &have);
+  check(fk_linear(a.data_ptr(), nullptr, b.data_ptr(), nullptr, 0, nullptr, c.data_ptr(), M, N, K, 0.f, ws, have,
+                  stream_of(a)));
+}
+
+// The tcgen05 path by name (M > 16 tokens), explicit workspace.
+void gemm_tc(TensorView x, TensorView w, TensorView y, TensorView workspace) {
+  require(x.size(0) > 16, "gemm_tc takes M > 16 tokens (M <= 16 runs the weight-streaming path: skinny_gemm)");
+  use(x);
+  check(fk_linear(x.data_ptr(), nullptr, w.data_ptr(), nullptr, 0, nullptr, y.data_ptr(), (int)x.size(0),
+                  (int)w.size(0), (int)x.size(1), 0.f, workspace.data_ptr(), nbytes(workspace), stream_of(x)));
+}
+
+void swiglu2(TensorView a, TensorView b, TensorView b1, TensorView c) {
+  use(a);
+  const int M = (int)a.size(0), N = (int)b.size(0), K = (int)a.size(1);
+  size_t need = 0, have = 0;
+  check(fk_linear_workspace_bytes(M, N, K, FK_LINEAR_SWIGLU, &need));
+  void* ws = module_workspace(a.device().device_id, need, &have);
+  check(fk_swiglu_gemm2(a.data_ptr(), b.data_ptr(), b1.data_ptr(), c.data_ptr(), M, N, K, ws, have, stream_of(a)));
+}
+
+// Single-launch decode attention: partial slots = o_partial.size(0) (>= 2);
+// counters int32 [B * Hkv], zero, left zero.
+void dec_attn_fused(TensorView q, TensorView k_cache, TensorView v_cache, TensorView cache_seqlens, TensorView out,
+                    TensorView lse, TensorView o_partial, TensorView lse_partial, TensorView counters,
+                    double softmax_scale) {
+  require(k_cache.ndim() == 4, "k_cache must be [B, Lmax, Hkv, D]");
+  use(q);
+  const int B = (int)k_cache.size(0), L = (int)k_cache.size(1), Hkv = (int)k_cache.size(2);
+  const int D = (int)k_cache.size(3);
+  const int Hq = (int)(q.ndim() == 4 ? q.size(2) : q.size(1));
+  const float scale = softmax_scale > 0 ? (float)softmax_scale : 1.0f / std::sqrt((float)D);
+  check(fk_dec_attn_fwd_fused(q.data_ptr(), (long long)Hq * D, k_cache.data_ptr(), v_cache.data_ptr(), nullptr,
+                              static_cast<const int32_t*>(cache_seqlens.data_ptr()), nullptr, out.data_ptr(), nullptr,
+                              0, static_cast<float*>(lse.data_ptr()), static_cast<float*>(o_partial.data_ptr()),
+                              static_cast<float*>(lse_partial.data_ptr()), static_cast<int32_t*>(counters.data_ptr()),
+                              B, L, 0, 0, Hq, Hkv, D, (int)o_partial.size(0), scale, stream_of(q)));
+}
+
+// Paged single-launch decode attention: k_pool / v_pool [num_blocks, block_size, Hkv, D],
+// block_table [B, max_blocks] int32.
+void dec_attn_paged(TensorView q, TensorView k_pool, TensorView v_pool, TensorView block_table,
+                    TensorView cache_seqlens, TensorView out, TensorView lse, TensorView o_partial,
+                    TensorView lse_partial, TensorView counters, double softmax_scale) {
+  require(k_pool.ndim() == 4 && block_table.ndim() == 2, "k_pool [NB, BS, Hkv, D], block_table [B, max_blocks]");
+  use(q);
+  const int NB = (int)k_pool.size(0), BS = (int)k_pool.size(1), Hkv = (int)k_pool.size(2), D = (int)k_pool.size(3);
+  const int B = (int)block_table.size(0), MB = (int)block_table.size(1);
+  const int Hq = (int)(q.ndim() == 4 ? q.size(2) : q.size(1));
+  const float scale = softmax_scale > 0 ? (float)softmax_scale : 1.0f / std::sqrt((float)D);
+  check(fk_dec_attn_fwd_fused(q.data_ptr(), (long long)Hq * D, k_pool.data_ptr(), v_pool.data_ptr(),
+                              static_cast<const int32_t*>(block_table.data_ptr()),
+                              static_cast<const int32_t*>(cache_seqlens.data_ptr()), nullptr, out.data_ptr(), nullptr,
+                              0, static_cast<float*>(lse.data_ptr()), static_cast<float*>(o_partial.data_ptr()),
+                              static_cast<float*>(lse_partial.data_ptr()), static_cast<int32_t*>(counters.data_ptr()),
+                              B, MB * BS, BS, NB, Hq, Hkv, D, (int)o_partial.size(0), scale, stream_of(q)));
+}
+
+// RMSNorm -> QKV projection whose epilogue appends the new K/V rows at
+// cache_seqlens[m] (contiguous caches [M, Lmax, Hkv, D]) and writes the advanced
+// lengths to seqlens_next. y [M, (Hq + 2 Hkv) * D]: q columns, then k, then v.
+void linear_kv_append(TensorView x, TensorView gamma, TensorView w, TensorView y, TensorView k_cache,
+                      TensorView v_cache, TensorView cache_seqlens, TensorView seqlens_next, int64_t num_heads_q,
+                      double eps, TensorView workspace) {
+  require(k_cache.ndim() == 4, "k_cache must be [M, Lmax, Hkv, D]");
+  use(x);
+  const int Hkv = (int)k_cache.size(2), D = (int)k_cache.size(3);
+  check(fk_linear_kv_append(x.data_ptr(), gamma.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0),
+                            (int)w.size(0), (int)x.size(1), (float)eps, k_cache.data_ptr(), v_cache.data_ptr(),
+                            nullptr, static_cast<const int32_t*>(cache_seqlens.data_ptr()),
+                            static_cast<int32_t*>(seqlens_next.data_ptr()), (int)num_heads_q * D,
+                            (int)(num_heads_q + Hkv) * D, Hkv, D, (int)k_cache.size(1), 0, workspace.data_ptr(),
+                            nbytes(workspace), stream_of(x)));
+}
+
 int64_t linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t swiglu) {
   size_t b = 0;
   check(fk_linear_workspace_bytes((int)M, (int)N, (int)K, swiglu ? FK_LINEAR_SWIGLU : 0, &b));
@@ -169,3 +275,9 @@ TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm, swiglu_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu_gemm2, swiglu_gemm2);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(lora_gemm, lora_gemm);
 TVM_FFI_DLL_EXPORT_TYPED_FUNC(linear_workspace_bytes, linear_workspace_bytes);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(gemm, gemm);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(gemm_tc, gemm_tc);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(swiglu2, swiglu2);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_fused, dec_attn_fused);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(dec_attn_paged, dec_attn_paged);
+TVM_FFI_DLL_EXPORT_TYPED_FUNC(linear_kv_append, linear_kv_append);

@@ -69,7 +69,8 @@ def test_tvm_ffi_module_loads_and_exports():
 
     mod = tvm_ffi_module.load()
     for name in ("dec_attn_splitkv_fwd", "dec_attn_combine", "dattn1", "skinny_gemm", "rmsnorm_linear",
-                 "swiglu_gemm", "swiglu_gemm2", "lora_gemm", "prefill_attn", "dattn2", "linear_workspace_bytes"):
+                 "swiglu_gemm", "swiglu_gemm2", "lora_gemm", "prefill_attn", "dattn2", "linear_workspace_bytes",
+                 "gemm", "gemm_tc", "swiglu2", "dec_attn_fused", "dec_attn_paged", "linear_kv_append"):
         assert getattr(mod, name) is not None
 
 

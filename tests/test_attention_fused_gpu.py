@@ -235,3 +235,33 @@ def test_starved_pipeline_times_out_in_every_consumer_warp():
     assert _native.device_error() == 0
     ref_out, ref_lse = oracle.decode_attention(q, k, v, lens)
     assert_attn_close(out, lse, ref_out, ref_lse)
+
+
+def test_tvm_ffi_single_launch_entries_match_python():
+    pytest.importorskip("tvm_ffi")
+    from fused_kernels_cutedsl_lib_b200 import tvm_ffi_module
+
+    mod = tvm_ffi_module.load()
+    torch.manual_seed(4)
+    B, L, Hq, Hkv, bs = 3, 512, 32, 8, 64
+    q = torch.randn(B, 1, Hq, 128, device="cuda").bfloat16()
+    k = torch.randn(B, L, Hkv, 128, device="cuda").bfloat16()
+    v = torch.randn(B, L, Hkv, 128, device="cuda").bfloat16()
+    lens = torch.tensor([512, 100, 0], dtype=torch.int32, device="cuda")
+    S = 5
+    ref = _run(q, k, v, lens, S, True, ctr=alloc_counters(B, Hkv, "cuda"))
+    out = torch.empty(B, 1, Hq, 128, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B, Hq, device="cuda")
+    o_p, l_p = alloc_partials(B, Hq, S, "cuda")
+    ctr = alloc_counters(B, Hkv, "cuda")
+    mod.dec_attn_fused(q, k, v, lens, out, lse, o_p, l_p, ctr, 0.0)
+    torch.cuda.synchronize()
+    _same(ref, (out, lse))
+    # paged: identity block table over the same cache
+    table = torch.arange(B * (L // bs), dtype=torch.int32, device="cuda").view(B, L // bs)
+    kp, vp = k.view(-1, bs, Hkv, 128), v.view(-1, bs, Hkv, 128)
+    out2 = torch.empty_like(out)
+    mod.dec_attn_paged(q, kp, vp, table, lens, out2, lse, o_p, l_p, ctr, 0.0)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, out)
+    assert int(ctr.abs().sum()) == 0

@@ -306,3 +306,66 @@ def test_linear_ex_strided_output_and_residual(M):
     ref = linear(x, w, residual=res_full[:, c0:c0 + N].contiguous())
     assert torch.equal(full[:, c0:c0 + N], ref)
     assert torch.all(full[:, :c0] == 7.0) and torch.all(full[:, c0 + N:] == 7.0)
+
+
+def test_tvm_ffi_reference_call_shapes_and_compile_cutedsl():
+    """TVM-FFI functions with the reference's call shapes (no workspace argument),
+    compile_cutedsl returning them, the named tcgen05 entry and the fused QKV +
+    KV-append entry: all equal to the ctypes path bit for bit."""
+    pytest.importorskip("tvm_ffi")
+    import tvm_ffi
+
+    from fused_kernels_cutedsl_lib_b200 import Gemm4SM90, Swiglu2SM90, compile_cutedsl, tvm_ffi_module
+    from fused_kernels_cutedsl_lib_b200.layer import linear_kv_append
+
+    mod = tvm_ffi_module.load()
+    for M in (3, 16, 96):
+        x, w = mk(M, 2048, 1024, seed=30 + M)
+        y = torch.empty(M, 2048, dtype=torch.bfloat16, device="cuda")
+        f = compile_cutedsl((x, w, y), Gemm4SM90(), False)
+        assert isinstance(f, tvm_ffi.Function)
+        f(x, w, y)
+        torch.cuda.synchronize()
+        assert torch.equal(y, linear(x, w))
+        s = torch.cuda.Stream()
+        fs = compile_cutedsl((x, w, y), Gemm4SM90(), True)
+        y.zero_()
+        fs(x, w, y, s)
+        s.synchronize()
+        assert torch.equal(y, linear(x, w))
+        if M > 16:
+            ws = alloc_workspace(int(mod.linear_workspace_bytes(M, 2048, 1024, 0)), "cuda")
+            y2 = torch.empty_like(y)
+            mod.gemm_tc(x, w, y2, ws)
+            torch.cuda.synchronize()
+            assert torch.equal(y2, y)
+    x, b = mk(8, 1024, 1024, seed=40)
+    b1 = mk(8, 1024, 1024, seed=41)[1]
+    c = torch.empty(8, 1024, dtype=torch.bfloat16, device="cuda")
+    compile_cutedsl((x, b, b1, c), Swiglu2SM90(), False)(x, b, b1, c)
+    torch.cuda.synchronize()
+    assert torch.equal(c, swiglu_gemm2(x, b, b1))
+    with pytest.raises(ValueError):
+        mod.gemm_tc(x, b, c, alloc_workspace(1 << 20, "cuda"))  # M <= 16 is not the tcgen05 path
+    # fused QKV projection + KV append through TVM-FFI vs ctypes
+    B, Hq, Hkv, L = 4, 8, 2, 64
+    x = torch.randn(B, 1024, device="cuda").bfloat16()
+    gam = gamma_of(1024)
+    wqkv = (0.02 * torch.randn((Hq + 2 * Hkv) * 128, 1024, device="cuda")).bfloat16()
+    outs = []
+    for use_tvm in (False, True):
+        kc = torch.zeros(B, L, Hkv, 128, dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        lens = torch.tensor([0, 5, 63, 64], dtype=torch.int32, device="cuda")
+        nxt = torch.zeros_like(lens)
+        y = torch.empty(B, wqkv.shape[0], dtype=torch.bfloat16, device="cuda")
+        ws = alloc_workspace(int(mod.linear_workspace_bytes(B, wqkv.shape[0], 1024, 0)), "cuda")
+        if use_tvm:
+            mod.linear_kv_append(x, gam, wqkv, y, kc, vc, lens, nxt, Hq, 1e-6, ws)
+        else:
+            linear_kv_append(x, wqkv, y, kc, vc, lens, nxt, Hq, Hkv, gamma=gam, eps=1e-6, workspace=ws)
+        torch.cuda.synchronize()
+        outs.append((y, kc, vc, nxt))
+    for a, b_ in zip(*outs):
+        assert torch.equal(a, b_)
+    assert outs[0][3].tolist() == [1, 6, 64, 64]

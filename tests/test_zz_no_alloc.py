@@ -10,6 +10,7 @@ import ctypes
 import pytest
 import torch
 
+import oracle
 from fused_kernels_cutedsl_lib_b200 import _native, configs, skinny_gemm
 
 pytestmark = pytest.mark.gpu
@@ -35,7 +36,9 @@ def _noalloc(x, w, y):
 
 
 def test_noalloc_matches_workspace_entry_point_twice():
-    # Two calls in a row with different shapes: the second must not see the first's scratch.
+    # Two calls in a row with different shapes: the second must not see the
+    # first's scratch. Each result is checked against the workspace entry point
+    # (the same kernel given caller scratch) and against the CPU oracle.
     for (M, N, K, seed) in [(16, 14336, 4096, 2), (3, 6144, 4096, 5)]:
         x, w = configs.gemm_inputs(M, N, K, seed)
         y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
@@ -44,6 +47,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         assert _native.device_error() == 0
         _close(y, ref)
+        _close(y, oracle.linear(x, w))
 
 
 def test_noalloc_rejects_sizes_beyond_limit():
