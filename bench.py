@@ -37,9 +37,10 @@ sys.path.insert(0, str(ROOT))
 # the others in their next collective).
 PG_TIMEOUT_S = 180
 
-# DRAM bytes (read + write) per launch of splitkv_fwd_kernel, from the ncu
-# capture summarised in profiles/splitkv_fwd_kernel_config2.md (small case scaled by KV bytes).
-NCU_TRAFFIC_BYTES_PER_LAUNCH = 4_615_000_000  # 542.3 MB at 537 MB of KV, scaled x8.51
+# DRAM bytes (read + write) per launch of the single-launch attention kernel: an
+# ncu capture of profile case attn_fused_small (541.5 MB at 536.9 MB of KV),
+# scaled by KV bytes to config 2 (x8.51; traffic grows in proportion).
+NCU_TRAFFIC_BYTES_PER_LAUNCH = 4_608_300_000  # 541.5 MB at 536.9 MB of KV, scaled x8.51
 
 
 def _peaks():

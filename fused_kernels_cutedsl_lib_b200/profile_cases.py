@@ -5,8 +5,8 @@ meaningful, a few GB at most), runs a few warm-up launches and then
 ``--launches`` launches of one kernel, and exits. The profiles/ summaries name
 the exact command, e.g.
 
-    ncu --set full --clock-control none -k regex:splitkv_fwd -s 2 -c 1 \
-        python -m fused_kernels_cutedsl_lib_b200.profile_cases attn_small
+    ncu --set full --clock-control none -k regex:splitkv_kernel -s 2 -c 1 \
+        python -m fused_kernels_cutedsl_lib_b200.profile_cases attn_fused_small
 """
 from __future__ import annotations
 
@@ -15,24 +15,84 @@ import argparse
 import torch
 
 
-def case_attn_small(launches: int):
-    """Decode attention B=16, 32q/8kv, every row at 8192 tokens: 537 MB of KV per launch."""
-    from . import alloc_partials, dec_attn_splitkv_fwd, default_num_splits
+def _attn_case(launches: int, single: bool, B=16, L=8192):
+    from . import alloc_counters, alloc_partials, dec_attn_splitkv_fwd, default_num_splits, fused_partial_slots
 
-    B, L, Hq, Hkv = 16, 8192, 32, 8
+    Hq, Hkv = 32, 8
     g = torch.Generator(device="cuda").manual_seed(0)
     q = torch.randn(B, 1, Hq, 128, device="cuda", generator=g).bfloat16()
     k = torch.randn(B, L, Hkv, 128, device="cuda", generator=g, dtype=torch.bfloat16)
     v = torch.randn(B, L, Hkv, 128, device="cuda", generator=g, dtype=torch.bfloat16)
     lens = torch.full((B,), L, dtype=torch.int32, device="cuda")
-    S = default_num_splits(B, Hkv, L)
+    S = fused_partial_slots(B, Hkv, L) if single else default_num_splits(B, Hkv, L)
     out = torch.empty(B, 1, Hq, 128, dtype=torch.bfloat16, device="cuda")
     lse = torch.empty(B, Hq, device="cuda")
     o_p, l_p = alloc_partials(B, Hq, S, "cuda")
+    ctr = alloc_counters(B, Hkv, "cuda")
     for _ in range(2 + launches):
-        dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, S)
+        dec_attn_splitkv_fwd(q, k, v, lens, out, lse, o_p, l_p, S, single_launch=single, counters=ctr)
     torch.cuda.synchronize()
-    print(f"attn_small: B={B} L={L} splits={S} kv_bytes={B * L * Hkv * 128 * 4}")
+    print(f"attn: B={B} L={L} single_launch={single} splits={S} kv_bytes={B * L * Hkv * 128 * 4}")
+
+
+def case_attn_small(launches: int):
+    """Decode attention, two-launch form (pass 1 + combine_kernel): B=16, 32q/8kv,
+    every row at 8192 tokens, 537 MB of KV per launch."""
+    _attn_case(launches, single=False)
+
+
+def case_attn_fused_small(launches: int):
+    """Decode attention, single-launch form (stream-K + in-kernel merge), same 537 MB case."""
+    _attn_case(launches, single=True)
+
+
+def case_dattn1(launches: int):
+    """Reference-semantics DAttn1 at the reference demo's shape scaled to exceed L2:
+    H=512 heads, M=16, P=1024 (K and V^T 512 MB together)."""
+    from .decoding_attention import DAttn1
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    H, M, P = 512, 16, 1024
+    Q = torch.randn(H, M, 128, device="cuda", generator=g).bfloat16()
+    K = torch.randn(H, P, 128, device="cuda", generator=g).bfloat16()
+    V = torch.randn(H, 128, P, device="cuda", generator=g).bfloat16()
+    O = torch.empty(H, M, 128, dtype=torch.bfloat16, device="cuda")
+    k = DAttn1()
+    for _ in range(2 + launches):
+        k(Q, K, V, O)
+    torch.cuda.synchronize()
+    print(f"dattn1: H={H} M={M} P={P}")
+
+
+def case_kv_append(launches: int):
+    """KV-cache append of 128 rows (config 5's batch) from a QKV output."""
+    from .layer import kv_append
+
+    B, L = 128, 8192 + 64
+    k = torch.zeros(B, L, 8, 128, dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros_like(k)
+    qkv = torch.randn(B, 6144, device="cuda").bfloat16()
+    for _ in range(2 + launches):
+        lens = torch.full((B,), 8192, dtype=torch.int32, device="cuda")
+        kv_append(qkv, k, v, lens, 32, 8)
+    torch.cuda.synchronize()
+    print("kv_append: B=128")
+
+
+def case_peer_barrier1(launches: int):
+    """The stage barrier kernel with one rank (no peer to wait for): its launch and fence cost."""
+    from . import _native
+
+    lib = _native.load()
+    buf = torch.zeros(16, dtype=torch.int32, device="cuda")
+    import ctypes
+
+    peers = (ctypes.c_void_p * 1)(buf.data_ptr() + 8)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2 + launches):
+        _native.check(lib.fk_peer_barrier(buf.data_ptr(), buf.data_ptr() + 8, peers, 0, 1, st))
+    torch.cuda.synchronize()
+    print("peer barrier, 1 rank")
 
 
 def _gemm_case(M, N, K, launches, kind="plain"):
@@ -155,6 +215,10 @@ def case_tp4_rank_step(launches: int):
 
 
 CASES = {
+    "attn_fused_small": case_attn_fused_small,
+    "dattn1": case_dattn1,
+    "kv_append": case_kv_append,
+    "peer_barrier1": case_peer_barrier1,
     "tp4_rank_step": case_tp4_rank_step,
     "prefill_d64": case_prefill_d64,
     "prefill_d128": case_prefill_d128,
