@@ -43,11 +43,15 @@ __global__ void barrier_kernel(BarrierArgs a) {
   if (threadIdx.x != 0) return;
   const int seq = *a.counter + 1;
   *a.counter = seq;
-  __threadfence_system();
+  // One release fence at system scope orders every earlier write of this
+  // stream (the stage's peer stores included) before the flag stores below,
+  // which are then plain relaxed stores: the fence + relaxed store pattern is a
+  // release, without a full sequentially consistent fence per peer.
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 #pragma unroll
   for (int r = 0; r < kMaxRanks; ++r) {
     if (r >= a.nranks || r == a.rank) continue;
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(a.peer_flags[r] + a.rank), "r"(seq) : "memory");
+    asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(a.peer_flags[r] + a.rank), "r"(seq) : "memory");
   }
   const uint64_t t0 = global_timer_ns();
   const uint64_t lim = wait_limit_ns(a.err);
@@ -63,7 +67,8 @@ __global__ void barrier_kernel(BarrierArgs a) {
       }
     }
   }
-  __threadfence_system();
+  // The acquire loads above order this thread after every peer's release; the
+  // next kernel on the stream starts after this grid completes.
 }
 
 }  // namespace peer
