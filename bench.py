@@ -406,8 +406,8 @@ def layer_measure(args, world, rank, dev, steps, warmup, tp_mode="peer", use_gra
     import torch.distributed as dist
 
     from fused_kernels_cutedsl_lib_b200 import _native
-    from fused_kernels_cutedsl_lib_b200.layer import (DecodeLayer, PeerTPDecodeLayer, TPDecodeLayer,
-                                                      random_layer_weights, shard_layer_weights)
+    from fused_kernels_cutedsl_lib_b200.layer import (DecodeLayer, HybridDecodeLayer, PeerTPDecodeLayer,
+                                                      TPDecodeLayer, random_layer_weights, shard_layer_weights)
 
     B, ctx, H, F, HQ, HKV = 128, 8192, 4096, 14336, 32, 8
     # every step appends one token per row: room for warm-up, capture and both timed loops
@@ -427,6 +427,8 @@ def layer_measure(args, world, rank, dev, steps, warmup, tp_mode="peer", use_gra
         # communication. x is this rank's rows of the global batch.
         layer = DecodeLayer(full, HQ, HKV)
         x = x[rank * Bl:(rank + 1) * Bl].contiguous()
+    elif world > 1 and tp_mode == "hybrid":
+        layer = HybridDecodeLayer(full, num_heads_q=HQ, num_heads_kv=HKV)
     elif world > 1 and tp_mode == "peer":
         layer = PeerTPDecodeLayer(shard_layer_weights(full, rank, world, HQ, HKV), num_heads_q=HQ, num_heads_kv=HKV)
     elif world > 1:
@@ -505,12 +507,67 @@ def layer_measure(args, world, rank, dev, steps, warmup, tp_mode="peer", use_gra
     # this library's kernels per step: QKV (rms_split, GEMM, reduce; KV append fused),
     # attention (1), O-proj (GEMM, reduce), gate/up (rms_split, GEMM, reduce), down
     # (GEMM, reduce); under TP with peer stores + 5 stage barriers and a separate append
-    launches = 11 if (world == 1 or dp) else (18 if tp_mode == "peer" else 13)
+    # hybrid: QKV and O-proj on B/P rows take the weight-streaming path (1 launch each) at B/P <= 16,
+    # the tcgen05 path (3 and 2) above; + attention, gate/up (3), down (2) and 3 barriers
+    launches = 11 if (world == 1 or dp) else {"peer": 18, "hybrid": 11 if Bl <= 16 else 14}.get(tp_mode, 13)
     del k, v, layer
     torch.cuda.empty_cache()
     return {"ms_per_step": ms, "e2e_ms_per_step": e2e_ms, "bytes_per_step": wbytes * (world if dp else 1) + kv_bytes,
             "launches_per_step": launches, "clocks": clk, "B": B, "ctx": ctx, "H": H, "F": F, "HQ": HQ, "HKV": HKV,
             "dp": dp}
+
+
+def hybrid_parity(world, rank, dev) -> dict:
+    """Small step of the hybrid layer against the single-GPU layer on the full
+    batch (two eager steps, the hybrid output fed back as the next input), within
+    the chained bf16 bound of the layer tests (max 5e-2, mean 1e-2 scaled error),
+    and one CUDA-graph replay bit-identical to an eager step on the same state."""
+    import torch.distributed as dist
+
+    from fused_kernels_cutedsl_lib_b200.layer import DecodeLayer, HybridDecodeLayer, random_layer_weights
+
+    B, L, H, F, HQ, HKV = 8 * world, 300, 4096, 14336, 32, 8
+    full = random_layer_weights(H, F, HQ, HKV, seed=21, device=dev)
+    g = torch.Generator(device=dev).manual_seed(22)
+    x = torch.randn(B, H, generator=g, device=dev).bfloat16()
+    k = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
+    v = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
+    lens = torch.tensor([200 + 5 * i for i in range(B)], dtype=torch.int32, device=dev)
+    Bl = B // world
+    rows = slice(rank * Bl, (rank + 1) * Bl)
+    kh, vh, lh = k[rows].clone(), v[rows].clone(), lens[rows].clone()  # the single-GPU layer appends to k, v
+    hyb = HybridDecodeLayer(full, num_heads_q=HQ, num_heads_kv=HKV)
+    single = DecodeLayer(full, HQ, HKV)
+    worst_max = worst_mean = 0.0
+    xh = x
+    for _ in range(2):
+        ys = single(xh, k, v, lens).clone()
+        yh = hyb(xh, kh, vh, lh).clone()
+        torch.cuda.synchronize()
+        e = (yh.float() - ys.float()).abs() / ys.float().abs().clamp_min(1.0)
+        worst_max, worst_mean = max(worst_max, e.max().item()), max(worst_mean, e.mean().item())
+        xh = yh
+    kg, vg, lg, xg = kh.clone(), vh.clone(), lh.clone(), xh.clone()
+    y_eager = hyb(xh, kh, vh, lh).clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        yg = hyb(xg, kg, vg, lg)
+    graph.replay()
+    torch.cuda.synchronize()
+    same = torch.equal(yg, y_eager) and torch.equal(kg, kh) and torch.equal(lg, lh)
+    del graph
+    dist.barrier()
+    hyb.close()
+    dist.barrier()
+    flags = torch.tensor([0.0 if same else 1.0, worst_max, worst_mean], dtype=torch.float64, device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    same = flags[0].item() == 0.0
+    worst_max, worst_mean = flags[1].item(), flags[2].item()
+    del full, k, v, single
+    torch.cuda.empty_cache()
+    return {"ok": bool(same and worst_max <= 5e-2 and worst_mean <= 1e-2), "graph_vs_eager_bitwise": bool(same),
+            "vs_single_gpu_max_scaled_err": round(worst_max, 5), "vs_single_gpu_mean_scaled_err": round(worst_mean, 6),
+            "case": f"B={B}, L~300, hidden 4096, ffn 14336, 32q/8kv: 2 eager steps + 1 graph replay"}
 
 
 def tp_parity(world, rank, dev) -> dict:
@@ -714,12 +771,15 @@ def run_extras(args, world, rank, dev, cpu: bool) -> dict:
     lo = {"ms_per_step": round(lay["ms_per_step"], 4), "tokens_per_s": round(lay["B"] / (lay["ms_per_step"] * 1e-3), 1),
           "e2e_ms_per_step": round(lay["e2e_ms_per_step"], 4),
           "parallelism": "single GPU" if world == 1 else (
-              f"dp{world}" if lay["dp"] else f"tp{world} GEMMs (column shards) + batch-sharded attention, "
-              + ("all-gathers in the kernels' epilogues over peer memory" if args.tp_mode == "peer" else "NCCL")),
+              f"dp{world}" if lay["dp"] else
+              (f"hybrid{world}: attention block batch-parallel (whole W_qkv, W_o), FFN column-parallel, "
+               "exchanges in the epilogues over peer memory, 3 stage barriers" if args.tp_mode == "hybrid" else
+               f"tp{world} GEMMs (column shards) + batch-sharded attention, "
+               + ("all-gathers in the kernels' epilogues over peer memory" if args.tp_mode == "peer" else "NCCL"))),
           "steps": args.layer_steps, "cuda_graph": True, "launches_per_step": lay["launches_per_step"],
           "roofline": _roof(lay["bytes_per_step"] / world, lay["ms_per_step"] * 1e3, peak, kind)}
     if world > 1:
-        lo["tp_parity"] = tp_parity(world, rank, dev)
+        lo["tp_parity"] = hybrid_parity(world, rank, dev) if args.tp_mode == "hybrid" else tp_parity(world, rank, dev)
     if cpu:
         lo["cpu_baseline"] = _cpu_layer()
     out["layer_ms_per_step"] = lo["ms_per_step"]
@@ -754,6 +814,8 @@ def run_layer(args):
                        "ffn": r["F"], "heads_q": r["HQ"], "heads_kv": r["HKV"],
                        "parallelism": "single GPU" if world == 1 else (
                            f"dp{world}: batch-sharded layer, weights replicated, no collective" if dp else
+                           f"hybrid{world}: attention block batch-parallel, FFN column-parallel, peer-memory "
+                           "exchanges" if args.tp_mode == "hybrid" else
                            f"tp{world} GEMMs + batch-sharded attention, all-gathers "
                            + ("in the GEMM / attention epilogues over peer memory" if args.tp_mode == "peer"
                               else "by NCCL")),
@@ -781,9 +843,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="layer workload: launch eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--tp-mode", choices=["peer", "nccl", "dp"], default="peer",
+    ap.add_argument("--tp-mode", choices=["peer", "nccl", "hybrid", "dp"], default="peer",
                     help="layer workload on N > 1 GPUs: tensor-parallel GEMMs with the all-gathers in the kernels "
-                         "over peer memory (peer) or by NCCL (nccl); or batch-parallel with replicated weights (dp)")
+                         "over peer memory (peer) or by NCCL (nccl); attention block batch-parallel with the FFN "
+                         "tensor-parallel over peer memory (hybrid); or batch-parallel with replicated weights (dp)")
     ap.add_argument("--workload", choices=["attention", "layer"], default="attention",
                     help="attention: config 2 split-KV decode attention (headline) plus, unless --no-extras, "
                          "configs 1, 3, 4 and the config-5 layer step as sub-objects of the same line; "

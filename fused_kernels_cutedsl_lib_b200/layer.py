@@ -472,3 +472,116 @@ class PeerTPDecodeLayer:
             self.arena.close()
             self.arena = None
             self._bufs.clear()
+
+
+class HybridDecodeLayer:
+    """Decode step on P GPUs: the attention block batch-parallel, the FFN tensor-parallel.
+
+    Each rank holds the attention-side weights whole (W_qkv, W_o, 84 MB at config
+    5) and a column shard of the FFN weights (W_gate_up, W_down: 352 MB / P).
+    Per step, with ``x`` the full [B, H] input (replicated):
+
+    1. RMSNorm -> QKV for this rank's B/P rows, KV append in the epilogue, attention
+       over the rows' own cache, O-projection + residual: all local, no exchange;
+       the O-projection's epilogue stores its rows into every rank's ``h`` buffer;
+    2. RMSNorm -> gate/up -> SwiGLU on all B rows for this rank's FFN columns,
+       stored into every rank's ``gu`` buffer at its column offset;
+    3. down-projection + residual for this rank's columns, stored into every
+       rank's ``y`` buffer.
+
+    A stage barrier separates the stages: 3 per step instead of the 5 of
+    :class:`PeerTPDecodeLayer`, and the attention-side GEMMs run on B/P rows of
+    whole weights (the weight-streaming path at B/P <= 16) instead of on N/P
+    columns of all rows. The exchanges are plain stores into CUDA IPC mappings
+    of the peers' buffers (no NCCL on the data path). Returns ``y`` [B, H], a
+    view into the shared arena valid until the next call.
+    """
+
+    def __init__(self, full: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
+        self.hidden = full.w_qkv.shape[1]
+        self.ffn = full.w_gate_up.shape[0] // 2
+        shard = shard_layer_weights(full, self.rank, self.world, num_heads_q, num_heads_kv)
+        self.w_attn = full  # gammas, W_qkv and W_o are used whole
+        self.w_gate_up, self.w_down = shard.w_gate_up, shard.w_down
+        self.c_lo = column_range(self.hidden, self.rank, self.world)[0]
+        self.f_lo = column_range(self.ffn, self.rank, self.world)[0]
+        self.arena = None
+        self._bufs: dict = {}
+
+    def _setup(self, B: int, Bl: int, L: int, device):
+        from .peer import PeerArena
+
+        key = (B, Bl, L)
+        if key in self._bufs:
+            return self._bufs[key]
+        H, F = self.hidden, self.ffn
+        if self.arena is None:
+            self.arena = PeerArena(2 * B * (2 * H + F) + (1 << 16), self.group)
+        a = self.arena
+        single, S = plan_attention(Bl, self.hkv, L)
+        o_p, l_p = alloc_partials(Bl, self.hq, S, device)
+        qkv_dim = self.w_attn.w_qkv.shape[0]
+        ws_need = max(workspace_bytes(m, n, k, sw) for m, n, k, sw in [
+            (Bl, qkv_dim, H, False), (Bl, H, self.hq * HEAD_DIM, False),
+            (B, self.w_gate_up.shape[0] // 2, H, True), (B, self.w_down.shape[0], F, False)])
+        bf = dict(dtype=torch.bfloat16, device=device)
+        b = dict(h=a.region(f"h{B}", (B, H)), gu=a.region(f"gu{B}", (B, F)), y=a.region(f"y{B}", (B, H)),
+                 qkv=torch.empty(Bl, qkv_dim, **bf), attn=torch.empty(Bl, self.hq * HEAD_DIM, **bf),
+                 lse=torch.empty(Bl, self.hq, dtype=torch.float32, device=device),
+                 lens_next=torch.empty(Bl, dtype=torch.int32, device=device),
+                 S=S, single=single, o_p=o_p, l_p=l_p, ctr=alloc_counters(Bl, self.hkv, device),
+                 ws=alloc_workspace(ws_need, device))
+        self._bufs[key] = b
+        return b
+
+    def _linear(self, x, w, y_ptr, ldy, peers, M, N, K, b, *, gamma=None, w_up=None, up_row_offset=0,
+                residual=None, ldr=0):
+        pp, n = _vp(peers)
+        ws = b["ws"]
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        _native.check(_native.load().fk_linear_ex(
+            ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(w_up) if w_up is not None else None,
+            up_row_offset, residual, ldr, y_ptr, ldy, pp, n, M, N, K, float(self.eps), ptr(ws), ws.numel(),
+            ctypes.c_void_p(st)))
+
+    def __call__(self, x, k_cache, v_cache, cache_seqlens):
+        """x [B, H] replicated; k/v caches and lengths hold this rank's B/P rows. Returns y [B, H] (arena view)."""
+        B, Bl, L = x.shape[0], k_cache.shape[0], k_cache.shape[1]
+        if Bl * self.world != B:
+            raise ValueError(f"batch {B} must split evenly: {Bl} rows per rank x {self.world} ranks")
+        b = self._setup(B, Bl, L, x.device)
+        w, a, H, F = self.w_attn, self.arena, self.hidden, self.ffn
+        B_ = str(B)
+        r0 = self.rank * Bl
+        x_loc = x[r0:r0 + Bl]
+        # 1. attention block on this rank's rows: QKV (+ KV append), attention, O-proj + residual
+        linear_kv_append(x_loc, w.w_qkv, b["qkv"], k_cache, v_cache, cache_seqlens, b["lens_next"], self.hq,
+                         self.hkv, gamma=w.gamma_attn, eps=self.eps, workspace=b["ws"])
+        attention_commit(b["qkv"], k_cache, v_cache, b["lens_next"], cache_seqlens, b["attn"], b["lse"], b["o_p"],
+                         b["l_p"], b["S"], self.hq, self.hkv, counters=b["ctr"], single_launch=b["single"])
+        self._linear(b["attn"], w.w_o, b["h"].data_ptr() + 2 * r0 * H, H, a.peer_ptrs("h" + B_, r0 * H), Bl, H,
+                     self.hq * HEAD_DIM, b, residual=x_loc.data_ptr(), ldr=x.stride(0))
+        a.barrier()
+        # 2. RMSNorm -> gate/up -> SwiGLU, this rank's FFN columns of all rows
+        fl = self.w_gate_up.shape[0] // 2
+        self._linear(b["h"], self.w_gate_up, b["gu"].data_ptr() + 2 * self.f_lo, F, a.peer_ptrs("gu" + B_, self.f_lo),
+                     B, fl, H, b, gamma=w.gamma_ffn, w_up=self.w_gate_up, up_row_offset=fl)
+        a.barrier()
+        # 3. down-projection + residual h, this rank's columns of all rows
+        self._linear(b["gu"], self.w_down, b["y"].data_ptr() + 2 * self.c_lo, H, a.peer_ptrs("y" + B_, self.c_lo),
+                     B, self.w_down.shape[0], F, b, residual=b["h"].data_ptr() + 2 * self.c_lo, ldr=H)
+        a.barrier()
+        return b["y"]
+
+    def close(self):
+        if self.arena is not None:
+            self.arena.close()
+            self.arena = None
+            self._bufs.clear()
