@@ -780,6 +780,14 @@ def run_extras(args, world, rank, dev, cpu: bool) -> dict:
           "roofline": _roof(lay["bytes_per_step"] / world, lay["ms_per_step"] * 1e3, peak, kind)}
     if world > 1:
         lo["tp_parity"] = hybrid_parity(world, rank, dev) if args.tp_mode == "hybrid" else tp_parity(world, rank, dev)
+        # the other decompositions of the same step, measured the same way
+        modes = {args.tp_mode: lo["ms_per_step"]}
+        for m in ("peer", "hybrid", "dp"):
+            if m not in modes:
+                r = layer_measure(args, world, rank, dev, steps=args.layer_steps, warmup=3, tp_mode=m, use_graph=True,
+                                  clocks_on=False)
+                modes[m] = round(r["ms_per_step"], 4)
+        lo["ms_per_step_by_mode"] = modes
     if cpu:
         lo["cpu_baseline"] = _cpu_layer()
     out["layer_ms_per_step"] = lo["ms_per_step"]

@@ -176,7 +176,7 @@ def _hybrid_worker(rank, world, port, q):
             x = torch.randn(B, H, generator=g, device=dev).bfloat16()
             k = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
             v = torch.randn(B, L, HKV, 128, generator=g, device=dev).bfloat16()
-            lens = torch.tensor([200 + 5 * i for i in range(B)], dtype=torch.int32, device=dev)
+            lens = torch.tensor([200 + (5 * i) % 90 for i in range(B)], dtype=torch.int32, device=dev)
             Bl = B // world
             rows = slice(rank * Bl, (rank + 1) * Bl)
             kh, vh, lh = k[rows].clone(), v[rows].clone(), lens[rows].clone()
