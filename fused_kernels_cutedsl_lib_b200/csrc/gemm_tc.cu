@@ -50,6 +50,10 @@ constexpr int WBOX = BM * 128;  // 16 KB
 constexpr int NORM_TILE = 128;  // tokens per launch with RMSNorm (hi + lo = 256 columns)
 constexpr size_t kSmemBudget = 227 * 1024;
 constexpr int kMaxGrid = 192;   // persistent grid bound (148 SMs on B200)
+// Output staging tile of the epilogue (16 tokens x 128 features, bf16): with
+// peer copies the outputs go out as 16-byte rows of 8 features instead of one
+// 2-byte element per lane.
+constexpr int STAGE_OUT = 16 * BM * 2;
 
 // Two TMA rings: a deep one for the weight tiles (streamed from HBM, long
 // latency) and a shallower one for the x tiles (re-read from L2 every k block,
@@ -60,7 +64,7 @@ struct Layout {
   static constexpr int W_BYTES = WBOX * (SWIGLU ? 2 : 1);
   static constexpr int X_BYTES = NMMA * 128;
   static constexpr int SX = X_BYTES >= 32768 ? (SWIGLU ? 2 : 3) : (X_BYTES >= 16384 ? 5 : 6);
-  static constexpr int SW_FIT = (int)((kSmemBudget - 4096 - (size_t)SX * X_BYTES) / (W_BYTES + 16));
+  static constexpr int SW_FIT = (int)((kSmemBudget - 4096 - STAGE_OUT - (size_t)SX * X_BYTES) / (W_BYTES + 16));
   // As many weight stages as shared memory holds: the kernel streams at the
   // rate of (weight bytes in flight per SM) / (HBM latency under load), so a
   // deeper ring is directly faster.
@@ -75,7 +79,8 @@ struct Layout {
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                    : TMEM_NEED <= 256 ? 256 : 512;
   // barriers: full + empty per W and x stage, acc_full[2], acc_empty[2], done; TMEM address
-  static constexpr size_t SMEM = 1024 + (size_t)SW * W_BYTES + (size_t)SX * X_BYTES + (2 * SW + 2 * SX + 5) * 8 + 16;
+  static constexpr size_t SMEM =
+      1024 + (size_t)SW * W_BYTES + (size_t)SX * X_BYTES + STAGE_OUT + (2 * SW + 2 * SX + 5) * 8 + 16;
 };
 
 __host__ __device__ constexpr int slot_floats(int nmma, bool swiglu) { return nmma * BM * (swiglu ? 2 : 1); }
@@ -94,6 +99,7 @@ struct Params {
   KvAppend kv;
   OutPlace out;       // row strides of y / residual and peer copies of y
   int has_ext;        // peers or KV append present (store_ext needed)
+  int vec_out;        // peers, no KV append, y / peers / ldy 16-byte aligned: staged 16-byte stores
   int starts[kMaxGrid + 1];  // starts[c] = c * total / G: first iteration of CTA c
 };
 
@@ -156,6 +162,36 @@ __device__ __forceinline__ void load_tokens(uint32_t trow, int c0, int Mp, float
   }
 }
 
+// Final value of output (m, col): RMSNorm scale, SwiGLU, residual, bf16 (not stored).
+__device__ __forceinline__ __nv_bfloat16 compute_out(const Params& p, int m, int col, float g, float u, bool swiglu) {
+  float rs = p.rstd ? __ldg(p.rstd + m) : 1.f;
+  float val = swiglu ? silu_f(g * rs) * (u * rs) : g * rs;
+  if (p.residual) val += __bfloat162float(p.residual[(size_t)m * p.out.ldr + col]);
+  return __float2bfloat16_rn(val);
+}
+
+// Writes a staged tile [ntok][128 features] (bf16, row-major in shared memory)
+// for tokens m0.. and features col0.. to y and every peer copy as 16-byte
+// rows of 8 features; a row running past N falls back to 2-byte stores.
+__device__ __forceinline__ void store_staged(const Params& p, const __nv_bfloat16* st, int ntok, int m0, int col0,
+                                             int tid, int nthreads) {
+  for (int i = tid; i < ntok * (BM / 8); i += nthreads) {
+    const int t = i / (BM / 8), f = (i % (BM / 8)) * 8;
+    const int m = m0 + t, col = col0 + f;
+    if (m >= p.M || col >= p.N) continue;
+    const size_t off = (size_t)m * p.out.ldy + col;
+    if (col + 8 <= p.N) {
+      const uint4 v = *reinterpret_cast<const uint4*>(st + t * BM + f);
+      *reinterpret_cast<uint4*>(p.y + off) = v;
+#pragma unroll
+      for (int k = 0; k < kMaxPeers; ++k)
+        if (k < p.out.npeers) *reinterpret_cast<uint4*>(p.out.peer_y[k] + off) = v;
+    } else {
+      for (int e = 0; col + e < p.N && e < 8; ++e) store_out_all(p.out, p.y, off + e, st[t * BM + f + e]);
+    }
+  }
+}
+
 // Final value of output (m, col): RMSNorm scale, SwiGLU, residual, bf16; stored to y.
 __device__ __forceinline__ __nv_bfloat16 store_out(const Params& p, int m, int col, float g, float u, bool swiglu) {
   float rs = p.rstd ? __ldg(p.rstd + m) : 1.f;
@@ -185,7 +221,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xring = smem + LY::X_RING;
-  uint64_t* full = reinterpret_cast<uint64_t*>(xring + SX * LY::X_BYTES);  // W ring [SW]
+  __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(xring + SX * LY::X_BYTES);  // [16][BM]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xring + SX * LY::X_BYTES + STAGE_OUT);  // W ring [SW]
   uint64_t* empty = full + SW;
   uint64_t* fullx = empty + SW;  // x ring [SX]
   uint64_t* emptyx = fullx + SX;
@@ -193,6 +230,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint64_t* done = acc_empty + 2;
   uint32_t* tmem_sm = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* epi_abort = reinterpret_cast<volatile int*>(tmem_sm + 1);  // an epilogue wait ran out
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -216,6 +254,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(done, 4);
+    *epi_abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -370,11 +409,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const long long seg_hi = min(it_end, (long long)(rb + 1) * p.KI);
     it = seg_hi;
     const bool full_rb = (seg_lo == (long long)rb * p.KI) && (seg_hi == (long long)(rb + 1) * p.KI);
-    if (!mbar_wait(&acc_full[buf], use_par, p.err, kDevErrMmaWait)) break;
+    // The four epilogue warps leave together on a time-out (they meet at named
+    // barriers in the staged-output path).
+    if (!mbar_wait_group(&acc_full[buf], use_par, p.err, kDevErrMmaWait, epi_abort)) break;
     tc_fence_after();
     if (et == 0) TC_TRACE(3 + 5 * (seg_lo != it_begin));
     const int col = rb * BM + row;
 
+    if (full_rb && p.vec_out) {
+      // Peer copies: stage 16 tokens x 128 features, then 16-byte rows.
+      for (int c0 = 0; c0 < mcols; c0 += 16) {
+        float a[16], u[16];
+        load_tokens<NORM>(trow, c0, p.Mp, a);
+        if (SWIGLU) load_tokens<NORM>(trow + NMMA, c0, p.Mp, u);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          ostage[i * BM + row] = (col < p.N && c0 + i < p.M) ? compute_out(p, c0 + i, col, a[i], SWIGLU ? u[i] : 0.f,
+                                                                           SWIGLU)
+                                                             : __float2bfloat16_rn(0.f);
+        named_bar_sync(2, EPI_THREADS);
+        store_staged(p, ostage, 16, c0, rb * BM, et, EPI_THREADS);
+        named_bar_sync(2, EPI_THREADS);  // the tile is rewritten by the next 16 tokens
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      continue;
+    }
     if (full_rb) {
       for (int c0 = 0; c0 < mcols; c0 += 16) {
         float a[16], u[16];
@@ -532,6 +593,17 @@ __global__ void __launch_bounds__(128) tc_reduce_kernel(Params p) {
     }
   }
   const int col = rb * BM + row;
+  if (p.vec_out) {
+    // Peer copies: stage 8 tokens x 128 features, then one 16-byte row per thread.
+    __shared__ __align__(16) __nv_bfloat16 st[8 * BM];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      st[i * BM + row] = (col < p.N && c0 + i < p.M) ? compute_out(p, c0 + i, col, g[i], u[i], SWIGLU)
+                                                     : __float2bfloat16_rn(0.f);
+    __syncthreads();
+    store_staged(p, st, 8, c0, rb * BM, row, BM);
+    return;
+  }
   if (col >= p.N) return;
   __nv_bfloat16 o[8];
 #pragma unroll
@@ -724,6 +796,11 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
     p.out.ldr = ldr;
     for (int i = 0; i < out0.npeers; ++i) p.out.peer_y[i] = out0.peer_y[i] + (size_t)m0 * ldy;
     p.has_ext = (out0.npeers > 0 || p.kv.k_cache != nullptr) ? 1 : 0;
+    {
+      bool al = out0.npeers > 0 && p.kv.k_cache == nullptr && ldy % 8 == 0 && ((uintptr_t)p.y & 15) == 0;
+      for (int i = 0; i < out0.npeers; ++i) al = al && ((uintptr_t)p.out.peer_y[i] & 15) == 0;
+      p.vec_out = al ? 1 : 0;
+    }
     CUtensorMap tmXa = tmX;
     if (lora) {
       const uint64_t adims[2] = {(uint64_t)ex->lora_rank, (uint64_t)mt};

@@ -308,6 +308,39 @@ def test_linear_ex_strided_output_and_residual(M):
     assert torch.all(full[:, :c0] == 7.0) and torch.all(full[:, c0 + N:] == 7.0)
 
 
+@pytest.mark.parametrize("M,N,kind", [(4, 512, "plain"), (100, 520, "plain"), (128, 1024, "rms"),
+                                      (64, 1792, "swiglu"), (200, 384, "plain")])
+def test_linear_ex_output_copies(M, N, kind):
+    """Output copies (the tensor-parallel layer's all-gather targets; here local
+    buffers stand in for peers' memory): every copy equals y bit for bit, y equals
+    the plain call, nothing outside the block is written. Covers the staged
+    16-byte path of the tcgen05 epilogue and reduction (M > 16, aligned) and its
+    2-byte fallback at a ragged N."""
+    import ctypes
+
+    K, ld = 1024, N + 256
+    sw = kind == "swiglu"
+    x, w = mk(M, 2 * N if sw else N, K, seed=M + N)
+    gam = gamma_of(K) if kind == "rms" else None
+    c0 = 128
+    outs = [torch.full((M, ld), 7.0, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    ws = alloc_workspace(workspace_bytes(M, N, K, sw), "cuda")
+    peers = (ctypes.c_void_p * 2)(outs[1].data_ptr() + 2 * c0, outs[2].data_ptr() + 2 * c0)
+    st = torch.cuda.current_stream().cuda_stream
+    _native.check(_native.load().fk_linear_ex(
+        x.data_ptr(), gam.data_ptr() if gam is not None else None, w.data_ptr(), w.data_ptr() if sw else None,
+        N if sw else 0, None, 0, outs[0].data_ptr() + 2 * c0, ld, peers, 2, M, N, K, 1e-6, ws.data_ptr(), ws.numel(),
+        ctypes.c_void_p(st)))
+    finish()
+    if sw:
+        ref = linear(x, w, w_up=w, up_row_offset=N)
+    else:
+        ref = linear(x, w, gamma=gam, eps=1e-6)
+    for o in outs:
+        assert torch.equal(o[:, c0:c0 + N], ref)
+        assert torch.all(o[:, :c0] == 7.0) and torch.all(o[:, c0 + N:] == 7.0)
+
+
 def test_tvm_ffi_reference_call_shapes_and_compile_cutedsl():
     """TVM-FFI functions with the reference's call shapes (no workspace argument),
     compile_cutedsl returning them, the named tcgen05 entry and the fused QKV +
