@@ -112,6 +112,17 @@ SIGNATURES: dict[str, tuple] = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _p],
     ),
     "fk_debug_attn_withhold_tile": (_c_int, [_c_int]),
+    "fk_peer_signal": (_c_int, [_p, _p, _c_int, _c_int, _p]),
+    "fk_linear_ex_wait": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _p, _c_int, _p, _c_int, _p, _c_int, _c_int, _c_int, _c_int, _c_float, _p,
+         ctypes.c_size_t, _p, _p, _c_int, _c_int, _p],
+    ),
+    "fk_kv_append_wait": (
+        _c_int,
+        [_p, ctypes.c_longlong, _c_int, _c_int, _p, _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p, _p, _c_int,
+         _c_int, _p],
+    ),
     "fk_rmsnorm_swiglu": (
         _c_int, [_p, _p, _p, _p, _c_int, _c_int, _c_int, _c_float, _p, ctypes.c_size_t, _p]),
 }

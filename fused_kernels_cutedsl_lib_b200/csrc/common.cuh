@@ -319,6 +319,36 @@ __device__ __forceinline__ void store_out_all(const OutPlace& o, __nv_bfloat16* 
     if (i < o.npeers) o.peer_y[i][off] = v;
 }
 
+// The wait half of a cross-GPU stage barrier, done by the kernel that consumes
+// the stage (fk_peer_signal did the other half): seq = *counter (advanced by
+// the signal kernel, which completed before this kernel passed
+// griddepcontrol.wait), then until flags[r] >= seq for every peer r. One
+// thread, bounded; counter null: no wait.
+struct PeerWait {
+  const int* counter;
+  const int* flags;
+  int rank, nranks;
+};
+
+__device__ __forceinline__ void peer_wait(const PeerWait& w, int* err) {
+  if (w.counter == nullptr) return;
+  const int seq = *reinterpret_cast<const volatile int*>(w.counter);
+  const uint64_t t0 = global_timer_ns();
+  const uint64_t lim = wait_limit_ns(err);
+  for (int r = 0; r < w.nranks; ++r) {
+    if (r == w.rank) continue;
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(w.flags + r) : "memory");
+      if (v - seq >= 0) break;
+      if (global_timer_ns() - t0 > lim) {
+        record_device_error(err, kDevErrFlagWait);
+        return;
+      }
+    }
+  }
+}
+
 // Extensions a linear call may carry besides its main operands.
 struct LinearExtras {
   KvAppend kv;                 // kv.k_cache null: none
@@ -326,6 +356,7 @@ struct LinearExtras {
   const void* lora_b;          // [N, rank] bf16
   int lora_rank;               // multiple of 8
   OutPlace out;                // ldy = ldr = 0, npeers = 0: dense local output
+  PeerWait wait;               // counter null: no cross-GPU wait before reading x
 };
 
 }  // namespace fk

@@ -100,6 +100,7 @@ struct Params {
   OutPlace out;       // row strides of y / residual and peer copies of y
   int has_ext;        // peers or KV append present (store_ext needed)
   int vec_out;        // peers, no KV append, y / peers / ldy 16-byte aligned: staged 16-byte stores
+  PeerWait wait;      // cross-GPU stage wait before x is read (counter null: none)
   int starts[kMaxGrid + 1];  // starts[c] = c * total / G: first iteration of CTA c
 };
 
@@ -309,6 +310,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tma_prefetch_desc(&tmX);
       const uint64_t pol_x = l2_policy_evict_last();
       asm volatile("griddepcontrol.wait;" ::: "memory");
+      // x may be the output of other GPUs' stage: wait for their signals (the
+      // epilogue writes only results that depend on x, so it is ordered after).
+      peer_wait(p.wait, p.err);
       int stage = 0;
       uint32_t phase = 0;
       for (long long it = it_begin; it < it_end; ++it) {
@@ -488,8 +492,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 __global__ void __launch_bounds__(256) rms_split_kernel(const __nv_bfloat16* __restrict__ x,
                                                         const __nv_bfloat16* __restrict__ gamma, float eps, int K,
                                                         int M, int Mp, __nv_bfloat16* __restrict__ xs,
-                                                        float* __restrict__ rstd) {
+                                                        float* __restrict__ rstd, PeerWait wait, int* err) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // let the GEMM start streaming W
+  if (wait.counter) {  // x is the output of other GPUs' stage: wait for their signals
+    if (threadIdx.x == 0) peer_wait(wait, err);
+    __syncthreads();
+  }
   const int m = blockIdx.x;
   uint4* hi = reinterpret_cast<uint4*>(xs + (size_t)m * K);
   uint4* lo = reinterpret_cast<uint4*>(xs + (size_t)(Mp + m) * K);
@@ -714,6 +722,7 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
   p.KI_main = KI_main;
   p.kv = {};
   if (ex) p.kv = ex->kv;
+  p.wait = ex ? ex->wait : PeerWait{};
   const OutPlace out0 = ex ? ex->out : OutPlace{};
   const int ldy = out0.ldy > 0 ? out0.ldy : N, ldr = out0.ldr > 0 ? out0.ldr : N;
   p.partials = reinterpret_cast<float*>(ws + kCounterBytes + tc_xs_bytes(K) + tc_rstd_bytes());
@@ -769,7 +778,7 @@ int tc_linear(const void* x, const void* gamma, const void* w, const void* w_up,
     if (norm) {
       const int Mp = tc::round16(mt);
       tc::rms_split_kernel<<<Mp, 256, 0, stream>>>(xt, static_cast<const __nv_bfloat16*>(gamma), eps, K, mt, Mp, xs,
-                                                   rstd);
+                                                   rstd, p.wait, p.err);
       FK_CHECK_CUDA(cudaGetLastError());
       p.Mp = Mp;
       p.rstd = rstd;

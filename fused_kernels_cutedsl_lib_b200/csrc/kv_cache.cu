@@ -17,8 +17,13 @@ namespace kv {
 __global__ void __launch_bounds__(128) append_kernel(const __nv_bfloat16* __restrict__ src, long long src_stride,
                                                      int k_col, int v_col, __nv_bfloat16* __restrict__ kc,
                                                      __nv_bfloat16* __restrict__ vc, const int* seqlens_in,
-                                                     int* seqlens_out, int Lmax, int row_elems) {
+                                                     int* seqlens_out, int Lmax, int row_elems, PeerWait wait,
+                                                     int* err) {
   const int b = blockIdx.x;
+  if (wait.counter) {  // src is the output of other GPUs' stage: wait for their signals
+    if (threadIdx.x == 0) peer_wait(wait, err);
+    __syncthreads();
+  }
   const int pos = seqlens_in[b];
   __syncthreads();  // every thread has read the length before it may be overwritten in place
   const bool ok = pos >= 0 && pos < Lmax;
@@ -83,9 +88,9 @@ extern "C" int fk_kv_append_paged(const void* src, long long src_row_stride, int
   return kOk;
 }
 
-extern "C" int fk_kv_append(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
-                            void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
-                            int max_seqlen, int num_heads_kv, int head_dim, void* stream) {
+static int kv_append_impl(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
+                          void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
+                          int max_seqlen, int num_heads_kv, int head_dim, void* stream, const PeerWait& wait) {
   FK_CHECK_ARG(src && k_cache && v_cache && cache_seqlens, "null tensor pointer");
   FK_CHECK_ARG(batch >= 1 && max_seqlen >= 1 && num_heads_kv >= 1 && head_dim >= 8, "sizes must be positive");
   const int row = num_heads_kv * head_dim;
@@ -93,11 +98,31 @@ extern "C" int fk_kv_append(const void* src, long long src_row_stride, int k_col
                "row length, stride and column offsets must be multiples of 8 elements");
   FK_CHECK_ARG(((uintptr_t)src & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
                "src and caches must be 16-byte aligned");
+  int* err = device_error_word();
+  if (!err) return fail(kErrCuda, "device error word unavailable");
   kv::append_kernel<<<batch, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(src), src_row_stride, k_col, v_col, static_cast<__nv_bfloat16*>(k_cache),
-      static_cast<__nv_bfloat16*>(v_cache), cache_seqlens, seqlens_out, max_seqlen, row);
+      static_cast<__nv_bfloat16*>(v_cache), cache_seqlens, seqlens_out, max_seqlen, row, wait, err);
   FK_CHECK_CUDA(cudaGetLastError());
   return kOk;
+}
+
+extern "C" int fk_kv_append(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
+                            void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
+                            int max_seqlen, int num_heads_kv, int head_dim, void* stream) {
+  return kv_append_impl(src, src_row_stride, k_col, v_col, k_cache, v_cache, cache_seqlens, seqlens_out, batch,
+                        max_seqlen, num_heads_kv, head_dim, stream, PeerWait{});
+}
+
+extern "C" int fk_kv_append_wait(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
+                                 void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
+                                 int max_seqlen, int num_heads_kv, int head_dim, const int32_t* wait_counter,
+                                 const int32_t* wait_flags, int rank, int nranks, void* stream) {
+  FK_CHECK_ARG(wait_counter && wait_flags, "null wait counter / flags");
+  FK_CHECK_ARG(nranks >= 1 && nranks <= kMaxPeers + 1 && rank >= 0 && rank < nranks, "bad rank / nranks");
+  const PeerWait pw{wait_counter, wait_flags, rank, nranks};
+  return kv_append_impl(src, src_row_stride, k_col, v_col, k_cache, v_cache, cache_seqlens, seqlens_out, batch,
+                        max_seqlen, num_heads_kv, head_dim, stream, pw);
 }
 
 namespace fk {

@@ -126,9 +126,10 @@ int fk_linear_kv_append(const void* x, const void* gamma, const void* w, void* y
 
 // General linear with output placement: y rows ldy apart (>= N), residual rows
 // ldr apart, and npeers more copies of y in other GPUs' memory (IPC mappings).
-int fk_linear_ex(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
-                 const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M, int N,
-                 int K, float eps, void* workspace, size_t workspace_bytes, void* stream) {
+static int linear_ex_impl(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
+                          const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M,
+                          int N, int K, float eps, void* workspace, size_t workspace_bytes, void* stream,
+                          const PeerWait& wait) {
   FK_CHECK_ARG(npeers >= 0 && npeers <= kMaxPeers, "npeers must be in [0, 7]");
   FK_CHECK_ARG(ldy == 0 || ldy >= N, "ldy must be 0 (dense) or >= N");
   FK_CHECK_ARG(ldr == 0 || ldr >= N, "ldr must be 0 (dense) or >= N");
@@ -140,8 +141,27 @@ int fk_linear_ex(const void* x, const void* gamma, const void* w, const void* w_
     FK_CHECK_ARG(peer_y && peer_y[i], "null peer output pointer");
     ex.out.peer_y[i] = static_cast<__nv_bfloat16*>(peer_y[i]);
   }
+  ex.wait = wait;
   return dispatch(x, gamma, w, w_up, up_row_offset, residual, y, M, N, K, eps, workspace, workspace_bytes, stream,
                   &ex);
+}
+
+int fk_linear_ex(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
+                 const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M, int N,
+                 int K, float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  return linear_ex_impl(x, gamma, w, w_up, up_row_offset, residual, ldr, y, ldy, peer_y, npeers, M, N, K, eps,
+                        workspace, workspace_bytes, stream, PeerWait{});
+}
+
+int fk_linear_ex_wait(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
+                      const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M, int N,
+                      int K, float eps, void* workspace, size_t workspace_bytes, const int32_t* wait_counter,
+                      const int32_t* wait_flags, int rank, int nranks, void* stream) {
+  FK_CHECK_ARG(wait_counter && wait_flags, "null wait counter / flags");
+  FK_CHECK_ARG(nranks >= 1 && nranks <= kMaxPeers + 1 && rank >= 0 && rank < nranks, "bad rank / nranks");
+  const PeerWait pw{wait_counter, wait_flags, rank, nranks};
+  return linear_ex_impl(x, gamma, w, w_up, up_row_offset, residual, ldr, y, ldy, peer_y, npeers, M, N, K, eps,
+                        workspace, workspace_bytes, stream, pw);
 }
 
 }  // extern "C"

@@ -31,6 +31,7 @@ struct BarrierArgs {
   int* local_flags;             // local [P]: written by the peers
   int* peer_flags[kMaxRanks];   // peer r's flags array (index rank is ours); entry `rank` unused
   int rank, nranks;
+  int wait;                     // 0: signal only (the next kernel waits, see PeerWait)
   int* err;
 };
 
@@ -53,6 +54,7 @@ __global__ void barrier_kernel(BarrierArgs a) {
     if (r >= a.nranks || r == a.rank) continue;
     asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(a.peer_flags[r] + a.rank), "r"(seq) : "memory");
   }
+  if (!a.wait) return;
   const uint64_t t0 = global_timer_ns();
   const uint64_t lim = wait_limit_ns(a.err);
   for (int r = 0; r < a.nranks; ++r) {
@@ -118,9 +120,9 @@ int fk_ipc_close(void* ptr) {
   return kOk;
 }
 
-int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer_flags, int rank, int nranks,
-                    void* stream) {
-  FK_CHECK_ARG(counter && local_flags && peer_flags, "null pointer");
+static int barrier_impl(int32_t* counter, int32_t* local_flags, int32_t* const* peer_flags, int rank, int nranks,
+                        void* stream, int wait) {
+  FK_CHECK_ARG(counter && (local_flags || !wait) && peer_flags, "null pointer");
   FK_CHECK_ARG(nranks >= 1 && nranks <= peer::kMaxRanks && rank >= 0 && rank < nranks, "bad rank / nranks");
   int* err = device_error_word();
   if (!err) return fail(kErrCuda, "device error word unavailable");
@@ -133,6 +135,7 @@ int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer
   }
   a.rank = rank;
   a.nranks = nranks;
+  a.wait = wait;
   a.err = err;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -145,6 +148,15 @@ int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer
   cfg.numAttrs = 1;
   FK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, peer::barrier_kernel, a));
   return kOk;
+}
+
+int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer_flags, int rank, int nranks,
+                    void* stream) {
+  return barrier_impl(counter, local_flags, peer_flags, rank, nranks, stream, 1);
+}
+
+int fk_peer_signal(int32_t* counter, int32_t* const* peer_flags, int rank, int nranks, void* stream) {
+  return barrier_impl(counter, nullptr, peer_flags, rank, nranks, stream, 0);
 }
 
 }  // extern "C"

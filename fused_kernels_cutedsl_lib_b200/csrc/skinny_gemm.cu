@@ -83,6 +83,7 @@ struct Params {
   KvAppend kv;
   OutPlace out;                   // row strides of y / residual and peer copies of y
   int has_ext;                    // peers or KV append present
+  PeerWait wait;                  // cross-GPU stage wait before x is read (counter null: none)
 };
 
 __device__ __forceinline__ long long it_start(const Params& p, int c) {
@@ -175,6 +176,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const long long pre_end = it_begin + STAGES < it_end ? it_begin + STAGES : it_end;
       for (long long it = it_begin; it < pre_end; ++it) load_w((int)(it - it_begin), it);
       asm volatile("griddepcontrol.wait;" ::: "memory");
+      // x may be the output of other GPUs' stage: wait for their signals. The
+      // consumers write y only after consuming x, so they are ordered after this.
+      peer_wait(p.wait, p.err);
       for (long long it = it_begin; it < pre_end; ++it) load_x((int)(it - it_begin), it);
       int stage = (int)((pre_end - it_begin) % STAGES);
       uint32_t phase = (pre_end - it_begin) >= STAGES ? 1u : 0u;
@@ -525,10 +529,12 @@ int skinny_linear(const void* x, const void* gamma, const void* w, const void* w
   p.KI_main = KI_main;
   p.kv = {};
   p.out = {};
+  p.wait = {};
   if (ex) {
     p.kv = ex->kv;
     p.kv.m_base = 0;
     p.out = ex->out;
+    p.wait = ex->wait;
   }
   if (p.out.ldy <= 0) p.out.ldy = N;
   if (p.out.ldr <= 0) p.out.ldr = N;

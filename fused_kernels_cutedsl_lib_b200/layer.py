@@ -368,13 +368,15 @@ class PeerTPDecodeLayer:
     nothing and can be captured in a CUDA graph.
     """
 
-    def __init__(self, weights: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6):
+    def __init__(self, weights: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6,
+                 fold_barriers=True):
         import torch.distributed as dist
 
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.fold_barriers = fold_barriers
         self.w = weights
         self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
         self.hidden = weights.w_qkv.shape[1]
@@ -411,16 +413,27 @@ class PeerTPDecodeLayer:
         return b
 
     def _linear(self, x, w, out_region, name, col_lo, n_total, b, *, gamma=None, w_up=None, up_row_offset=0,
-                residual=None, ldr=0):
+                residual=None, ldr=0, wait=False):
         M, K = x.shape
         N = w.shape[0] - up_row_offset if w_up is not None else w.shape[0]
         peers, n = _vp(self.arena.peer_ptrs(name, col_lo))
         ws = b["ws"]
         st = torch.cuda.current_stream(x.device).cuda_stream
-        _native.check(_native.load().fk_linear_ex(
-            ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(w_up) if w_up is not None else None,
-            up_row_offset, residual, ldr, out_region.data_ptr() + 2 * col_lo, n_total, peers, n, M, N, K,
-            float(self.eps), ptr(ws), ws.numel(), ctypes.c_void_p(st)))
+        args = (ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(w_up) if w_up is not None else None,
+                up_row_offset, residual, ldr, out_region.data_ptr() + 2 * col_lo, n_total, peers, n, M, N, K,
+                float(self.eps), ptr(ws), ws.numel())
+        if wait:
+            _native.check(_native.load().fk_linear_ex_wait(*args, *self.arena.wait_args(), ctypes.c_void_p(st)))
+        else:
+            _native.check(_native.load().fk_linear_ex(*args, ctypes.c_void_p(st)))
+
+    def _stage_end(self):
+        """Between stages: signal only (the next stage's first kernel waits) when
+        folding barriers, else the full barrier kernel."""
+        if self.fold_barriers:
+            self.arena.signal()
+        else:
+            self.arena.barrier()
 
     def __call__(self, x, k_cache, v_cache, cache_seqlens):
         """x [B, H] replicated; k/v caches and lengths hold this rank's B/P rows. Returns y [B, H] (arena view)."""
@@ -433,11 +446,17 @@ class PeerTPDecodeLayer:
         st = torch.cuda.current_stream(x.device).cuda_stream
         # QKV: this rank's column block of every row, pushed to all ranks
         self._linear(x, w.w_qkv, b["qkv"], "qkv" + B_, self.qkv_lo, self.n_qkv, b, gamma=w.gamma_attn)
-        a.barrier()
+        self._stage_end()
         # attention on this rank's batch rows (q read in place), rows pushed to all ranks
         r0 = self.rank * Bl
         my_qkv = b["qkv"][r0:r0 + Bl]
-        kv_append(my_qkv, k_cache, v_cache, cache_seqlens, self.hq, self.hkv)
+        if self.fold_barriers:
+            _native.check(_native.load().fk_kv_append_wait(
+                ptr(my_qkv), my_qkv.stride(0), self.hq * HEAD_DIM, (self.hq + self.hkv) * HEAD_DIM, ptr(k_cache),
+                ptr(v_cache), ptr(cache_seqlens), ptr(cache_seqlens), Bl, k_cache.shape[1], self.hkv, HEAD_DIM,
+                *a.wait_args(), ctypes.c_void_p(st)))
+        else:
+            kv_append(my_qkv, k_cache, v_cache, cache_seqlens, self.hq, self.hkv)
         hd = self.hq * HEAD_DIM
         if b["single"]:
             attn_fused_launch(ptr(my_qkv), my_qkv.stride(0), k_cache, v_cache, cache_seqlens,
@@ -451,20 +470,21 @@ class PeerTPDecodeLayer:
                 ptr(my_qkv), my_qkv.stride(0), ptr(k_cache), ptr(v_cache), ptr(cache_seqlens),
                 b["attn"].data_ptr() + 2 * r0 * hd, peers, n, ptr(b["lse"]), ptr(b["o_p"]), ptr(b["l_p"]), Bl, L,
                 self.hq, self.hkv, HEAD_DIM, b["S"], 1.0 / math.sqrt(HEAD_DIM), ctypes.c_void_p(st)))
-        a.barrier()
+        self._stage_end()
+        fold = self.fold_barriers
         # O-projection + residual x
         self._linear(b["attn"], w.w_o, b["h"], "h" + B_, self.c_lo, H, b, residual=x.data_ptr() + 2 * self.c_lo,
-                     ldr=H)
-        a.barrier()
+                     ldr=H, wait=fold)
+        self._stage_end()
         # RMSNorm -> gate/up -> SwiGLU
         fl = w.w_gate_up.shape[0] // 2
         self._linear(b["h"], w.w_gate_up, b["gu"], "gu" + B_, self.f_lo, F, b, gamma=w.gamma_ffn,
-                     w_up=w.w_gate_up, up_row_offset=fl)
-        a.barrier()
+                     w_up=w.w_gate_up, up_row_offset=fl, wait=fold)
+        self._stage_end()
         # down-projection + residual h
         self._linear(b["gu"], w.w_down, b["y"], "y" + B_, self.c_lo, H, b,
-                     residual=b["h"].data_ptr() + 2 * self.c_lo, ldr=H)
-        a.barrier()
+                     residual=b["h"].data_ptr() + 2 * self.c_lo, ldr=H, wait=fold)
+        a.barrier()  # full barrier: y is complete on every rank when the call returns
         return b["y"]
 
     def close(self):
@@ -497,13 +517,15 @@ class HybridDecodeLayer:
     view into the shared arena valid until the next call.
     """
 
-    def __init__(self, full: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6):
+    def __init__(self, full: LayerWeights, group=None, num_heads_q=32, num_heads_kv=8, eps=1e-6,
+                 fold_barriers=True):
         import torch.distributed as dist
 
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.fold_barriers = fold_barriers
         self.hq, self.hkv, self.eps = num_heads_q, num_heads_kv, eps
         self.hidden = full.w_qkv.shape[1]
         self.ffn = full.w_gate_up.shape[0] // 2
@@ -542,14 +564,22 @@ class HybridDecodeLayer:
         return b
 
     def _linear(self, x, w, y_ptr, ldy, peers, M, N, K, b, *, gamma=None, w_up=None, up_row_offset=0,
-                residual=None, ldr=0):
+                residual=None, ldr=0, wait=False):
         pp, n = _vp(peers)
         ws = b["ws"]
         st = torch.cuda.current_stream(x.device).cuda_stream
-        _native.check(_native.load().fk_linear_ex(
-            ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(w_up) if w_up is not None else None,
-            up_row_offset, residual, ldr, y_ptr, ldy, pp, n, M, N, K, float(self.eps), ptr(ws), ws.numel(),
-            ctypes.c_void_p(st)))
+        args = (ptr(x), ptr(gamma) if gamma is not None else None, ptr(w), ptr(w_up) if w_up is not None else None,
+                up_row_offset, residual, ldr, y_ptr, ldy, pp, n, M, N, K, float(self.eps), ptr(ws), ws.numel())
+        if wait:
+            _native.check(_native.load().fk_linear_ex_wait(*args, *self.arena.wait_args(), ctypes.c_void_p(st)))
+        else:
+            _native.check(_native.load().fk_linear_ex(*args, ctypes.c_void_p(st)))
+
+    def _stage_end(self):
+        if self.fold_barriers:
+            self.arena.signal()
+        else:
+            self.arena.barrier()
 
     def __call__(self, x, k_cache, v_cache, cache_seqlens):
         """x [B, H] replicated; k/v caches and lengths hold this rank's B/P rows. Returns y [B, H] (arena view)."""
@@ -568,16 +598,17 @@ class HybridDecodeLayer:
                          b["l_p"], b["S"], self.hq, self.hkv, counters=b["ctr"], single_launch=b["single"])
         self._linear(b["attn"], w.w_o, b["h"].data_ptr() + 2 * r0 * H, H, a.peer_ptrs("h" + B_, r0 * H), Bl, H,
                      self.hq * HEAD_DIM, b, residual=x_loc.data_ptr(), ldr=x.stride(0))
-        a.barrier()
+        self._stage_end()
+        fold = self.fold_barriers
         # 2. RMSNorm -> gate/up -> SwiGLU, this rank's FFN columns of all rows
         fl = self.w_gate_up.shape[0] // 2
         self._linear(b["h"], self.w_gate_up, b["gu"].data_ptr() + 2 * self.f_lo, F, a.peer_ptrs("gu" + B_, self.f_lo),
-                     B, fl, H, b, gamma=w.gamma_ffn, w_up=self.w_gate_up, up_row_offset=fl)
-        a.barrier()
+                     B, fl, H, b, gamma=w.gamma_ffn, w_up=self.w_gate_up, up_row_offset=fl, wait=fold)
+        self._stage_end()
         # 3. down-projection + residual h, this rank's columns of all rows
         self._linear(b["gu"], self.w_down, b["y"].data_ptr() + 2 * self.c_lo, H, a.peer_ptrs("y" + B_, self.c_lo),
-                     B, self.w_down.shape[0], F, b, residual=b["h"].data_ptr() + 2 * self.c_lo, ldr=H)
-        a.barrier()
+                     B, self.w_down.shape[0], F, b, residual=b["h"].data_ptr() + 2 * self.c_lo, ldr=H, wait=fold)
+        a.barrier()  # full barrier: y is complete on every rank when the call returns
         return b["y"]
 
     def close(self):

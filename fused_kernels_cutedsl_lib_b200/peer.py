@@ -102,6 +102,18 @@ class PeerArena:
             ctypes.c_void_p(self._counter), ctypes.c_void_p(self.base + self._flags_off), self._peer_flags,
             self.rank, self.world, ctypes.c_void_p(st)))
 
+    def signal(self, stream=None):
+        """The signal half of :meth:`barrier`: advance the counter and store it into
+        every peer's flag slot, without waiting. The next launch on the stream must
+        do the wait (``*_wait`` entry points with :meth:`wait_args`)."""
+        st = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
+        _native.check(_native.load().fk_peer_signal(
+            ctypes.c_void_p(self._counter), self._peer_flags, self.rank, self.world, ctypes.c_void_p(st)))
+
+    def wait_args(self) -> tuple:
+        """(counter, flags, rank, world) for the ``*_wait`` entry points."""
+        return (ctypes.c_void_p(self._counter), ctypes.c_void_p(self.base + self._flags_off), self.rank, self.world)
+
     def close(self):
         lib = _native.load()
         for r, b in enumerate(self.bases):

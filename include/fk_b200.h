@@ -331,6 +331,26 @@ FK_API int fk_ipc_close(void* ptr);
 FK_API int fk_peer_barrier(int32_t* counter, int32_t* local_flags, int32_t* const* peer_flags, int rank,
                            int nranks, void* stream);
 
+/* The two halves of fk_peer_barrier, for a barrier whose wait is done by the
+ * kernel that consumes the stage. fk_peer_signal: one thread advances *counter
+ * to seq, fences at system scope and stores seq into peer_flags[r][rank] for
+ * every r != rank; it does not wait. The next launch on the stream then waits
+ * (bounded, 1 s) until local flags[r] >= *counter for every peer before it
+ * reads data the peers wrote: fk_linear_ex_wait (in the kernel that loads x:
+ * the GEMM's token-load warp, or the RMSNorm prologue) and fk_kv_append_wait.
+ * Otherwise as fk_linear_ex / fk_kv_append. Removes the separate waiting kernel
+ * between stages: the wait overlaps the next GEMM's weight prefetch. */
+FK_API int fk_peer_signal(int32_t* counter, int32_t* const* peer_flags, int rank, int nranks, void* stream);
+FK_API int fk_linear_ex_wait(const void* x, const void* gamma, const void* w, const void* w_up, int up_row_offset,
+                             const void* residual, int ldr, void* y, int ldy, void* const* peer_y, int npeers, int M,
+                             int N, int K, float eps, void* workspace, size_t workspace_bytes,
+                             const int32_t* wait_counter, const int32_t* wait_flags, int rank, int nranks,
+                             void* stream);
+FK_API int fk_kv_append_wait(const void* src, long long src_row_stride, int k_col, int v_col, void* k_cache,
+                             void* v_cache, const int32_t* cache_seqlens, int32_t* seqlens_out, int batch,
+                             int max_seqlen, int num_heads_kv, int head_dim, const int32_t* wait_counter,
+                             const int32_t* wait_flags, int rank, int nranks, void* stream);
+
 /* Skinny GEMM y = x W^T (1 <= M <= 16, N <= 524288) that allocates nothing:
  * its stream-K scratch is a fixed ~2.7 MB device array inside this library
  * (one per GPU, kept until process exit) instead of a caller workspace. For
