@@ -792,7 +792,6 @@ def run_extras(args, world, rank, dev, cpu: bool) -> dict:
         lo["cpu_baseline"] = _cpu_layer()
     out["layer_ms_per_step"] = lo["ms_per_step"]
     out["layer"] = lo
-    out["extras_wall_s"] = round(time.perf_counter() - t0, 1)
     return out
 
 
