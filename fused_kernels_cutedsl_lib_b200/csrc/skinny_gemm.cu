@@ -62,7 +62,10 @@ struct Layout {
   static constexpr int TX_BYTES = W_BYTES + 2 * XBOX_BYTES + (NORM ? KT * 2 : 0);
   static constexpr int STAGE_BYTES = ((G_OFF + (NORM ? KT * 2 : 0)) + 1023) / 1024 * 1024;
   static constexpr int STAGES_FIT = (int)((kSmemBudget - 2048) / STAGE_BYTES);
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  // RMSNorm at M <= 8: a 4-stage ring (measured 16.9 vs 17.5 us back to back for
+  // the 50 MB QKV projection at M = 1; no change at M = 16 or without RMSNorm).
+  static constexpr int STAGES_CAP = (NORM && NT == 1) ? 4 : 8;
+  static constexpr int STAGES = STAGES_FIT > STAGES_CAP ? STAGES_CAP : STAGES_FIT;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 2 * STAGES * 8 + 16 * 4 + 16;
 };
 
