@@ -47,17 +47,18 @@ def chunk_tokens(max_seqlen: int, num_splits: int) -> int:
 def default_num_splits(batch: int, num_heads_kv: int, max_seqlen: int,
                        total_tokens: int | None = None, num_sms: int = 148) -> int:
     """Pick num_splits: the largest chunk of {1024, 512, 256, 128, 64} tokens
-    that still gives at least one work unit (row, kv head, split) per SM.
+    that still gives work units (row, kv head, split) for at least three
+    quarters of the SMs.
 
     Large chunks amortise each unit's setup (q load, pipeline fill) and keep
     the merge of the splits short; at config 2's ~1.1 M tokens 1024-token
-    chunks still give ~8700 units, dealt round-robin. The pass-1 grid keeps two
-    CTAs resident per SM (shared memory allows two), so a count just above one
-    unit per SM leaves some resident CTAs idle; at config 1 (B = 4, L = 4096)
-    the rule gives 8 splits = 256 units for 296 resident CTAs, every unit
-    running in the first wave. Measured at config 1: 4-8 splits take 18-19 us
-    per call back to back (two-launch form), 64 splits (the earlier "4 units
-    per resident CTA" rule) 36.5 us; configs 1 and 2 are the measured shapes.
+    chunks still give ~8700 units, dealt round-robin. At config 1 (B = 4,
+    L = 4096) the rule gives 4 splits = 128 units, one per SM on 128 of the 148
+    SMs, each streaming 512 KB. Measured there in one call (two-launch form):
+    4 splits 21.5 us isolated / 16.8 us back to back, 8 splits (256 units,
+    the earlier one-unit-per-SM rule) 21.5 / 17.5 us, 16 splits 25.6 / 20.1 us,
+    64 splits (an older "4 units per resident CTA" rule) 36.5 us back to back;
+    configs 1 and 2 are the measured shapes.
 
     ``total_tokens`` (sum of the true lengths) sharpens the count for ragged
     batches. Callers whose lengths live on the GPU (the decode layer) leave it
@@ -69,7 +70,7 @@ def default_num_splits(batch: int, num_heads_kv: int, max_seqlen: int,
     chunk = TILE_TOKENS
     for c in (1024, 512, 256, 128, 64):
         units = num_heads_kv * max(1, -(-total // c))
-        if units >= num_sms:
+        if 4 * units >= 3 * num_sms:
             chunk = c
             break
     return max(1, -(-max_seqlen // chunk))

@@ -80,20 +80,21 @@ def test_batch_parallel_layer_equals_the_whole_batch():
 
 
 def test_default_num_splits_pins_the_measured_shapes():
-    """The split rule at the measured shapes: config 1 takes 8 splits (512-token
-    chunks, 256 units), config 2 takes 32 (1024-token chunks) with or without its
+    """The split rule at the measured shapes: config 1 takes 4 splits (1024-token
+    chunks, 128 units), config 2 takes 32 (1024-token chunks) with or without its
     true token count, and a case too small for even 64-token chunks to give one
     unit per SM falls back to 64-token chunks."""
     from fused_kernels_cutedsl_lib_b200 import chunk_tokens, configs, default_num_splits
 
-    assert default_num_splits(4, 8, 4096) == 8
-    assert chunk_tokens(4096, 8) == 512
+    assert default_num_splits(4, 8, 4096) == 4
+    assert chunk_tokens(4096, 4) == 1024
     c2 = configs.ATTN_CONFIG2
     lens = configs.attn_seqlens(c2)
     assert default_num_splits(64, 8, 32768, int(lens.sum())) == 32
     assert default_num_splits(64, 8, 32768) == 32
-    # 2 rows x 1 kv head x 4096 tokens: 128 units at 64-token chunks < 148 SMs
-    assert default_num_splits(2, 1, 4096) == 64
+    # 1 row x 1 kv head x 4096 tokens: 64 units even at 64-token chunks, below the threshold
+    assert default_num_splits(1, 1, 4096) == 64
+    assert default_num_splits(1, 1, 4096) == 64
     assert chunk_tokens(4096, 64) == 64
     # every split count gives chunks that are multiples of the 64-token tile
     for L in (1, 63, 64, 65, 1000, 4096, 32768):
@@ -104,11 +105,11 @@ def test_default_num_splits_pins_the_measured_shapes():
 
 def test_plan_attention_picks_the_form_by_work_per_cta():
     """Config 1 (7 padded tiles per resident CTA) takes the two-launch form with
-    8 chunks; config 2 and the decode layer's batches take the single launch
+    4 chunks; config 2 and the decode layer's batches take the single launch
     with enough partial slots; every single-launch plan has >= 2 slots."""
     from fused_kernels_cutedsl_lib_b200 import fused_partial_slots, plan_attention
 
-    assert plan_attention(4, 8, 4096) == (False, 8)
+    assert plan_attention(4, 8, 4096) == (False, 4)
     assert plan_attention(64, 8, 32768) == (True, 4)
     assert plan_attention(128, 8, 8256)[0]
     for B in (1, 2, 16, 64, 128, 1024):
