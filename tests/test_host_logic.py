@@ -83,7 +83,7 @@ def test_default_num_splits_pins_the_measured_shapes():
     """The split rule at the measured shapes: config 1 takes 4 splits (1024-token
     chunks, 128 units), config 2 takes 32 (1024-token chunks) with or without its
     true token count, and a case too small for even 64-token chunks to give one
-    unit per SM falls back to 64-token chunks."""
+    unit for three quarters of the SMs falls back to 64-token chunks."""
     from fused_kernels_cutedsl_lib_b200 import chunk_tokens, configs, default_num_splits
 
     assert default_num_splits(4, 8, 4096) == 4
@@ -93,7 +93,6 @@ def test_default_num_splits_pins_the_measured_shapes():
     assert default_num_splits(64, 8, 32768, int(lens.sum())) == 32
     assert default_num_splits(64, 8, 32768) == 32
     # 1 row x 1 kv head x 4096 tokens: 64 units even at 64-token chunks, below the threshold
-    assert default_num_splits(1, 1, 4096) == 64
     assert default_num_splits(1, 1, 4096) == 64
     assert chunk_tokens(4096, 64) == 64
     # every split count gives chunks that are multiples of the 64-token tile
